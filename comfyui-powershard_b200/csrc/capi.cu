@@ -1,0 +1,283 @@
+// extern "C" entry points of libps_b200.so (declared in include/ps_b200.h):
+// argument validation, TMA descriptor encoding and kernel launches.
+#include "ps_b200.h"
+#include "internal.h"
+
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+namespace psb {
+
+namespace {
+thread_local char g_msg[512] = "";
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// The kernels are compiled for sm_100a only; refuse other devices up front.
+int check_device() {
+  static int verdict[64] = {0};  // 0 unknown, 1 ok, 2 unsupported
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
+  if (dev >= 0 && dev < 64 && verdict[dev] == 1) return PS_B200_OK;
+  int major = 0, minor = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e != cudaSuccess) return set_cuda_error("cudaDeviceGetAttribute", e);
+  const bool ok = major == 10 && minor == 0;
+  if (dev >= 0 && dev < 64) verdict[dev] = ok ? 1 : 2;
+  if (!ok)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "libps_b200 is built for sm_100a; device %d is sm_%d%d", dev, major,
+                     minor);
+  return PS_B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool is16bit(int dtype) { return dtype == PS_B200_BF16 || dtype == PS_B200_FP16; }
+
+// 5-D map over [batch][seg][row][head][d] with a (64 x 1 x 128 x 1 x 1) box:
+// one 64-column, 128-row half tile with 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, bool fp16, int head_dim, int heads, int seg_rows, int segs,
+             int batch, const int64_t st[4]) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(PS_B200_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  // Byte strides of the head, row, segment and batch axes.  Axes of extent 1
+  // get the span of the axes below them so the map stays well formed.
+  int64_t sh = st[3] * 2, sr = st[2] * 2, ss = st[1] * 2, sb = st[0] * 2;
+  if (heads == 1) sh = int64_t(head_dim) * 2;
+  if (seg_rows == 1) sr = sh * heads;
+  if (segs == 1) ss = sr * seg_rows;
+  if (batch == 1) sb = ss * segs;
+  const int64_t strides_b[4] = {sh, sr, ss, sb};
+  for (int i = 0; i < 4; ++i)
+    if (strides_b[i] <= 0 || strides_b[i] % 16 != 0 || strides_b[i] >= (int64_t(1) << 40))
+      return set_error(PS_B200_ERR_INVALID, "stride %lld bytes of axis %d is not a positive multiple of 16",
+                       (long long)strides_b[i], 4 - i);
+  cuuint64_t dims[5] = {cuuint64_t(head_dim), cuuint64_t(heads), cuuint64_t(seg_rows), cuuint64_t(segs),
+                        cuuint64_t(batch)};
+  cuuint64_t strides[4] = {cuuint64_t(sh), cuuint64_t(sr), cuuint64_t(ss), cuuint64_t(sb)};
+  cuuint32_t box[5] = {64, 1, 128, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PS_B200_ERR_INVALID, "cuTensorMapEncodeTiled failed with CUresult %d", int(r));
+  return PS_B200_OK;
+}
+
+void tile_plan(int seg_rows, int len, int& full_segs, int& tiles_per_seg, int& num_tiles) {
+  full_segs = len / seg_rows;
+  tiles_per_seg = (seg_rows + 127) / 128;
+  const int rem = len - full_segs * seg_rows;
+  num_tiles = full_segs * tiles_per_seg + (rem + 127) / 128;
+}
+
+struct SegTensor {
+  const void* ptr;
+  int64_t st[4];
+  int heads;  // extent of the head axis in the map
+};
+
+int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v, void* out,
+                     const int64_t out_st[4], int dtype, int out_dtype, int batch, int grid_heads, int group,
+                     int head_dim,
+                     int seg_rows_q, int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k,
+                     float softmax_scale, int* status, void* stream) {
+  if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "attention supports bf16 and fp16 only");
+  if (out_dtype != dtype && out_dtype != PS_B200_FP32)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "attention output must be fp32 or the input dtype");
+  if (head_dim != 128) return set_error(PS_B200_ERR_UNSUPPORTED, "attention supports head_dim 128 only (got %d)", head_dim);
+  if (batch < 0 || grid_heads < 0 || len_q < 0 || len_k < 0 || group < 1)
+    return set_error(PS_B200_ERR_INVALID, "negative size");
+  if (batch == 0 || grid_heads == 0 || len_q == 0) return PS_B200_OK;
+  if (len_k == 0) return set_error(PS_B200_ERR_INVALID, "empty key set");
+  if (seg_rows_q <= 0 || segs_q <= 0 || seg_rows_k <= 0 || segs_k <= 0)
+    return set_error(PS_B200_ERR_INVALID, "segment geometry must be positive");
+  if (int64_t(seg_rows_q) * segs_q < len_q || int64_t(seg_rows_k) * segs_k < len_k)
+    return set_error(PS_B200_ERR_INVALID, "len exceeds segments * seg_rows");
+  if (batch > 65535 || grid_heads > 65535) return set_error(PS_B200_ERR_UNSUPPORTED, "batch/heads above 65535");
+  if (!std::isfinite(softmax_scale)) return set_error(PS_B200_ERR_INVALID, "softmax_scale must be finite");
+  if (!q.ptr || !k.ptr || !v.ptr || !out) return set_error(PS_B200_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(q.ptr) || !aligned16(k.ptr) || !aligned16(v.ptr) || !aligned16(out))
+    return set_error(PS_B200_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  for (int i = 0; i < 4; ++i)
+    if (out_st[i] < 0 || out_st[i] % 8 != 0)
+      return set_error(PS_B200_ERR_INVALID, "output strides must be non-negative multiples of 8 elements");
+  if (status && (reinterpret_cast<uintptr_t>(status) & 3u) != 0)
+    return set_error(PS_B200_ERR_INVALID, "status word must be 4-byte aligned");
+  if (int rc = check_device()) return rc;
+  const bool fp16 = dtype == PS_B200_FP16;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map(&tq, q.ptr, fp16, head_dim, q.heads, seg_rows_q, segs_q, batch, q.st)) return rc;
+  if (int rc = make_map(&tk, k.ptr, fp16, head_dim, k.heads, seg_rows_k, segs_k, batch, k.st)) return rc;
+  if (int rc = make_map(&tv, v.ptr, fp16, head_dim, v.heads, seg_rows_k, segs_k, batch, v.st)) return rc;
+  AttnArgs a{};
+  a.out = out;
+  for (int i = 0; i < 4; ++i) a.o_stride[i] = out_st[i];
+  a.seg_rows_q = seg_rows_q;
+  a.len_q = len_q;
+  tile_plan(seg_rows_q, len_q, a.q_full_segs, a.q_tiles_per_seg, a.num_q_tiles);
+  a.seg_rows_k = seg_rows_k;
+  a.len_k = len_k;
+  tile_plan(seg_rows_k, len_k, a.kv_full_segs, a.kv_tiles_per_seg, a.num_kv_tiles);
+  a.group = group;
+  a.scale_log2 = static_cast<float>(double(softmax_scale) * 1.4426950408889634);
+  a.out_fp32 = out_dtype == PS_B200_FP32;
+  a.status = status;
+  return launch_attention(tq, tk, tv, a, grid_heads, batch, fp16, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_cuda_error(const char* what, cudaError_t err) {
+  return set_error(PS_B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+}  // namespace psb
+
+using namespace psb;
+
+extern "C" {
+
+int ps_b200_abi_version(void) { return PS_B200_ABI_VERSION; }
+
+const char* ps_b200_last_error(void) { return psb::g_msg; }
+
+int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                    const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,
+                    int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
+                    int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream) {
+  if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
+  if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
+      int64_t(heads_per_rank) * world < heads || head_dim <= 0)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent prepass geometry");
+  if (head_dim % 8 != 0) return set_error(PS_B200_ERR_UNSUPPORTED, "head_dim must be a multiple of 8");
+  if (int64_t(heads) * head_dim > 8192)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "heads*head_dim above 8192 is not supported");
+  if (seg_rows == 0) return PS_B200_OK;
+  if (!send || !aligned16(send)) return set_error(PS_B200_ERR_INVALID, "send buffer null or not 16-byte aligned");
+  if (n_local > 0) {
+    const void* xs[3] = {x_q, x_k, x_v};
+    for (int i = 0; i < 3; ++i)
+      if (!xs[i] || !aligned16(xs[i]) || !x_row_strides || x_row_strides[i] % 8 != 0 || x_row_strides[i] < 0)
+        return set_error(PS_B200_ERR_INVALID, "projection inputs must be 16-byte aligned with row strides %% 8 == 0");
+    if (norm_rope) {
+      if (!w_qnorm || !w_knorm || !aligned16(w_qnorm) || !aligned16(w_knorm))
+        return set_error(PS_B200_ERR_INVALID, "norm weights null or not 16-byte aligned");
+      if (w_dtype != dtype && w_dtype != PS_B200_FP32)
+        return set_error(PS_B200_ERR_UNSUPPORTED, "norm weights must be fp32 or the input dtype");
+      if (!freqs || !aligned16(freqs) || freqs_row_stride % 4 != 0 || freqs_row_stride < 0)
+        return set_error(PS_B200_ERR_INVALID, "freqs must be 16-byte aligned with a row stride %% 4 == 0");
+      if (!std::isfinite(eps) || eps < 0.f) return set_error(PS_B200_ERR_INVALID, "eps must be finite and >= 0");
+    }
+  }
+  if (int rc = check_device()) return rc;
+  PrepassArgs a{};
+  a.x[0] = x_q;
+  a.x[1] = x_k;
+  a.x[2] = x_v;
+  for (int i = 0; i < 3; ++i) a.x_row_stride[i] = x_row_strides ? x_row_strides[i] : 0;
+  a.w[0] = w_qnorm;
+  a.w[1] = w_knorm;
+  a.w_fp32 = w_dtype == PS_B200_FP32;
+  a.freqs = freqs;
+  a.freqs_row_stride = freqs_row_stride;
+  a.send = send;
+  a.world = world;
+  a.n_local = n_local;
+  a.seg_rows = seg_rows;
+  a.heads = heads;
+  a.heads_per_rank = heads_per_rank;
+  a.head_dim = head_dim;
+  a.eps = eps;
+  a.norm_rope = norm_rope;
+  return launch_prepass(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
+}
+
+int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                     const void* v, const int64_t v_strides[4], void* out, const int64_t out_strides[4],
+                     int dtype, int out_dtype, int batch, int heads_q, int heads_kv, int head_dim, int seg_rows_q,
+                     int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k, float softmax_scale,
+                     int* status, void* stream) {
+  if (!q_strides || !k_strides || !v_strides || !out_strides) return set_error(PS_B200_ERR_INVALID, "null strides");
+  if (heads_kv <= 0 || heads_q < 0 || heads_q % heads_kv != 0)
+    return set_error(PS_B200_ERR_INVALID, "heads_q must be a positive multiple of heads_kv");
+  SegTensor tq{q, {q_strides[0], q_strides[1], q_strides[2], q_strides[3]}, heads_q};
+  SegTensor tk{k, {k_strides[0], k_strides[1], k_strides[2], k_strides[3]}, heads_kv};
+  SegTensor tv{v, {v_strides[0], v_strides[1], v_strides[2], v_strides[3]}, heads_kv};
+  return attention_common(tq, tk, tv, out, out_strides, dtype, out_dtype, batch, heads_q, heads_q / heads_kv, head_dim,
+                          seg_rows_q, segs_q, len_q, seg_rows_k, segs_k, len_k, softmax_scale, status, stream);
+}
+
+int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
+                             int total, int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
+                             int* status, void* stream) {
+  if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
+      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
+  if (total == 0 || heads_valid == 0) return PS_B200_OK;
+  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows;
+  const int64_t block = n * h * D;  // one [seg_rows][h][D] block
+  const char* base = static_cast<const char*>(recv);
+  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
+  const int64_t out_st[4] = {int64_t(world) * block, block, h * D, D};  // elements of out_dtype
+  SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows, world, total,
+                          seg_rows, world, total, softmax_scale, status, stream);
+}
+
+int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
+                   int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream) {
+  if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "unpack supports bf16 and fp16 inputs only");
+  if (out_dtype != dtype && out_dtype != PS_B200_FP32)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "unpack output must be fp32 or the input dtype");
+  if (world < 1 || n_local < 0 || n_local > seg_rows || heads < 1 || heads_per_rank < 1 ||
+      int64_t(heads_per_rank) * world < heads || head_dim <= 0 || head_dim % 8 != 0)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent unpack geometry");
+  if (int64_t(n_local) * heads * (head_dim / 8) >= (int64_t(1) << 31))
+    return set_error(PS_B200_ERR_UNSUPPORTED, "unpack size above 2^31 vectors");
+  if (n_local == 0) return PS_B200_OK;
+  if (!recv || !out || !aligned16(recv) || !aligned16(out) || out_row_stride % 8 != 0 || out_row_stride < 0)
+    return set_error(PS_B200_ERR_INVALID, "unpack buffers must be 16-byte aligned, row stride %% 8 == 0");
+  if (int rc = check_device()) return rc;
+  UnpackArgs a{};
+  a.recv = recv;
+  a.out = out;
+  a.out_row_stride = out_row_stride;
+  a.world = world;
+  a.n_local = n_local;
+  a.seg_rows = seg_rows;
+  a.heads = heads;
+  a.heads_per_rank = heads_per_rank;
+  a.head_dim = head_dim;
+  a.out_fp32 = out_dtype == PS_B200_FP32;
+  return launch_unpack(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

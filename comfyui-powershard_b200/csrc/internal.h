@@ -1,0 +1,62 @@
+// Internal declarations shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace psb {
+
+// Arguments of the attention kernel that are not tensor maps.
+struct AttnArgs {
+  void* out;             // output element (batch 0, seg 0, row 0, head 0, d 0)
+  int64_t o_stride[4];   // batch, segment, row, head strides in elements (d stride 1)
+  int seg_rows_q;        // rows per query segment
+  int len_q;             // valid query rows over all segments
+  int q_full_segs;       // len_q / seg_rows_q
+  int q_tiles_per_seg;   // ceil(seg_rows_q / 128)
+  int num_q_tiles;       // query tiles with at least one valid row
+  int seg_rows_k;
+  int len_k;
+  int kv_full_segs;
+  int kv_tiles_per_seg;
+  int num_kv_tiles;
+  int group;             // query heads per key/value head (GQA)
+  float scale_log2;      // softmax_scale * log2(e)
+  int out_fp32;          // 1: output fp32, 0: output in the input 16-bit type
+  int* status;           // device status word (0 = ok), may be null
+};
+
+int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const AttnArgs& args, int heads_q, int batch, bool fp16, cudaStream_t stream);
+
+struct PrepassArgs {
+  const void* x[3];        // q, k, v projection outputs, [n_local][heads*head_dim]
+  int64_t x_row_stride[3]; // elements between consecutive tokens
+  const void* w[2];        // RMSNorm weights of q and k, [heads*head_dim]
+  int w_fp32;              // 1: weights are fp32, 0: same 16-bit type as x
+  const float* freqs;      // [n_local][head_dim/2][2][2] fp32
+  int64_t freqs_row_stride;// floats between consecutive tokens
+  void* send;              // [world][3][seg_rows][heads_per_rank][head_dim]
+  int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
+  float eps;
+  int norm_rope;           // 1: RMSNorm + RoPE on q and k, 0: plain pack
+};
+
+int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);
+
+struct UnpackArgs {
+  const void* recv;        // [world][seg_rows][heads_per_rank][head_dim]
+  void* out;               // [n_local][heads][head_dim] (row stride below)
+  int64_t out_row_stride;  // elements between consecutive tokens of out
+  int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
+  int out_fp32;            // 1: write fp32, 0: same 16-bit type as recv
+};
+
+int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream);
+
+// Error bookkeeping (thread-local message, returned code).
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t err);
+
+}  // namespace psb

@@ -1,0 +1,248 @@
+// HBM-bound kernels around the attention: the fused q/k RMSNorm + RoPE +
+// Ulysses pack ("pre-pass") and the receive-side head->sequence unpack.
+//
+// Pre-pass, one CTA per token row of the send segment (seg_rows CTAs):
+//   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)      (RMSNorm, full width)
+//         out[2j], out[2j+1] = F[j] @ (y[2j], y[2j+1])           (interleaved RoPE)
+//   v   : copied.
+// Each result goes straight to its slot of the all-to-all send buffer
+// [world][3][seg_rows][heads_per_rank][head_dim]: global head g lands in
+// destination block g / heads_per_rank at head slot g % heads_per_rank.
+// Rows past the local token count and heads past `heads` are written as
+// zeros (they are the zero padding of the reference's packing).
+// All loads/stores are 16-byte vectors; a token row of q/k stays in registers
+// between the sum-of-squares reduction and the normalisation.
+#include "internal.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace psb {
+namespace pre {
+
+constexpr int kThreads = 128;
+constexpr int kMaxVec = 8;  // 8 vectors of 8 elements per thread: width <= 8192
+
+template <bool kFp16>
+__device__ __forceinline__ float to_f(uint16_t v) {
+  if constexpr (kFp16) {
+    return __half2float(__ushort_as_half(v));
+  } else {
+    return __bfloat162float(__ushort_as_bfloat16(v));
+  }
+}
+
+template <bool kFp16>
+__device__ __forceinline__ uint16_t from_f(float f) {
+  if constexpr (kFp16) {
+    return __half_as_ushort(__float2half_rn(f));
+  } else {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4& v, uint16_t (&e)[8]) {
+  e[0] = v.x & 0xffff;
+  e[1] = v.x >> 16;
+  e[2] = v.y & 0xffff;
+  e[3] = v.y >> 16;
+  e[4] = v.z & 0xffff;
+  e[5] = v.z >> 16;
+  e[6] = v.w & 0xffff;
+  e[7] = v.w >> 16;
+}
+
+__device__ __forceinline__ uint4 pack8(const uint16_t (&e)[8]) {
+  uint4 v;
+  v.x = e[0] | (static_cast<uint32_t>(e[1]) << 16);
+  v.y = e[2] | (static_cast<uint32_t>(e[3]) << 16);
+  v.z = e[4] | (static_cast<uint32_t>(e[5]) << 16);
+  v.w = e[6] | (static_cast<uint32_t>(e[7]) << 16);
+  return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red[] may still be read from the previous call
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+template <bool kFp16>
+__global__ void __launch_bounds__(kThreads) prepass_kernel(const PrepassArgs a) {
+  __shared__ float red[kThreads / 32];
+  const int i = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int D = a.head_dim;
+  const int h = a.heads_per_rank;
+  const int vph = D >> 3;             // vectors per head
+  const int nvec = a.heads * vph;     // vectors per token row
+  uint16_t* send = static_cast<uint16_t*>(a.send);
+  const int64_t block_elems = static_cast<int64_t>(a.seg_rows) * h * D;  // one [seg_rows][h][D] block
+  auto slot = [&](int kind, int g, int dd) -> int64_t {
+    const int dst = g / h;
+    const int j = g - dst * h;
+    return (static_cast<int64_t>(dst) * 3 + kind) * block_elems + static_cast<int64_t>(i) * h * D +
+           static_cast<int64_t>(j) * D + dd;
+  };
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+
+  if (i >= a.n_local) {  // token padding of the last ranks: zeros for every head
+    const int total = a.world * h * vph;
+    for (int kind = 0; kind < 3; ++kind)
+      for (int v = tid; v < total; v += kThreads) {
+        const int g = v / vph;
+        *reinterpret_cast<uint4*>(send + slot(kind, g, (v - g * vph) * 8)) = zero;
+      }
+    return;
+  }
+
+  const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
+#pragma unroll
+  for (int kind = 0; kind < 3; ++kind) {
+    const uint16_t* x = static_cast<const uint16_t*>(a.x[kind]) + static_cast<int64_t>(i) * a.x_row_stride[kind];
+    const bool normed = kind < 2 && a.norm_rope;
+    uint4 xv[kMaxVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxVec; ++u) {
+      const int v = tid + u * kThreads;
+      if (v < nvec) {
+        xv[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(v) * 8));
+        if (normed) {
+          uint16_t e[8];
+          unpack8(xv[u], e);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float f = to_f<kFp16>(e[q]);
+            ss = fmaf(f, f, ss);
+          }
+        }
+      }
+    }
+    float r = 1.f;
+    if (normed) {
+      const float total = block_sum(ss, red);
+      const float mean = __fdiv_rn(total, static_cast<float>(a.heads * D));
+      r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxVec; ++u) {
+      const int v = tid + u * kThreads;
+      if (v >= nvec) continue;
+      const int g = v / vph;
+      const int dd = (v - g * vph) * 8;
+      uint4 outv = xv[u];
+      if (normed) {
+        uint16_t e[8];
+        unpack8(xv[u], e);
+        float y[8];
+        if (a.w_fp32) {
+          const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + v * 8);
+          const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r), w[q])));
+        } else {
+          uint16_t we[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + v * 8)), we);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r), to_f<kFp16>(we[q]))));
+        }
+        // RoPE: pair p of this vector is pair (dd/2 + p) of the head.
+        const float4* fp = reinterpret_cast<const float4*>(frow) + (dd >> 1);
+        uint16_t o[8];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float4 F = __ldg(fp + p);  // {F00, F01, F10, F11}
+          const float x0 = y[2 * p], x1 = y[2 * p + 1];
+          o[2 * p] = from_f<kFp16>(__fadd_rn(__fmul_rn(F.x, x0), __fmul_rn(F.y, x1)));
+          o[2 * p + 1] = from_f<kFp16>(__fadd_rn(__fmul_rn(F.z, x0), __fmul_rn(F.w, x1)));
+        }
+        outv = pack8(o);
+      }
+      *reinterpret_cast<uint4*>(send + slot(kind, g, dd)) = outv;
+    }
+  }
+  // Head padding: slots of heads [heads, world*h) are zero.
+  const int padded = (a.world * h - a.heads) * vph;
+  for (int kind = 0; kind < 3; ++kind)
+    for (int v = tid; v < padded; v += kThreads) {
+      const int g = a.heads + v / vph;
+      *reinterpret_cast<uint4*>(send + slot(kind, g, (v % vph) * 8)) = zero;
+    }
+}
+
+constexpr int kUnpackThreads = 256;
+
+template <bool kOutFp32, bool kFp16>
+__global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs a) {
+  const int D = a.head_dim;
+  const int h = a.heads_per_rank;
+  const int vph = D >> 3;
+  const int per_token = a.heads * vph;
+  const int total = a.n_local * per_token;
+  for (int idx = blockIdx.x * kUnpackThreads + threadIdx.x; idx < total; idx += gridDim.x * kUnpackThreads) {
+    const int i = idx / per_token;
+    const int rem = idx - i * per_token;
+    const int g = rem / vph;
+    const int dd = (rem - g * vph) * 8;
+    const int src = g / h;
+    const int j = g - src * h;
+    const uint16_t* in = static_cast<const uint16_t*>(a.recv) +
+                         ((static_cast<int64_t>(src) * a.seg_rows + i) * h + j) * D + dd;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(in));
+    const int64_t o = static_cast<int64_t>(i) * a.out_row_stride + static_cast<int64_t>(g) * D + dd;
+    if constexpr (kOutFp32) {
+      uint16_t e[8];
+      unpack8(v, e);
+      float4* out = reinterpret_cast<float4*>(static_cast<float*>(a.out) + o);
+      out[0] = make_float4(to_f<kFp16>(e[0]), to_f<kFp16>(e[1]), to_f<kFp16>(e[2]), to_f<kFp16>(e[3]));
+      out[1] = make_float4(to_f<kFp16>(e[4]), to_f<kFp16>(e[5]), to_f<kFp16>(e[6]), to_f<kFp16>(e[7]));
+    } else {
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + o) = v;
+    }
+  }
+}
+
+}  // namespace pre
+
+int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
+  using namespace pre;
+  if (a.seg_rows == 0) return 0;
+  const dim3 grid(a.seg_rows), block(kThreads);
+  if (fp16)
+    prepass_kernel<true><<<grid, block, 0, stream>>>(a);
+  else
+    prepass_kernel<false><<<grid, block, 0, stream>>>(a);
+  const cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? 0 : set_cuda_error("prepass launch", err);
+}
+
+int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream) {
+  using namespace pre;
+  const int64_t total = static_cast<int64_t>(a.n_local) * a.heads * (a.head_dim / 8);
+  if (total == 0) return 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total + kUnpackThreads - 1) / kUnpackThreads;
+  const int blocks = static_cast<int>(want < sms * 8LL ? want : sms * 8LL);
+  if (a.out_fp32) {
+    if (fp16) unpack_kernel<true, true><<<blocks, kUnpackThreads, 0, stream>>>(a);
+    else unpack_kernel<true, false><<<blocks, kUnpackThreads, 0, stream>>>(a);
+  } else {
+    if (fp16) unpack_kernel<false, true><<<blocks, kUnpackThreads, 0, stream>>>(a);
+    else unpack_kernel<false, false><<<blocks, kUnpackThreads, 0, stream>>>(a);
+  }
+  const cudaError_t err = cudaGetLastError();
+  return err == cudaSuccess ? 0 : set_cuda_error("unpack launch", err);
+}
+
+}  // namespace psb

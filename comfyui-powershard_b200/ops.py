@@ -1,0 +1,164 @@
+"""Tensor-level wrappers of the three device steps (one C-ABI call each).
+
+Each wrapper checks devices, dtypes, shapes and contiguity, then calls the
+matching ``ps_b200_*`` entry point on the current CUDA stream.  None of them
+allocates: callers pass every output buffer.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .partition import UlyssesGeometry
+
+
+class DeviceStatus:
+    """Device int32 status word of the attention kernel plus a lazy host check.
+
+    The kernel writes a non-zero code (PS_B200_DEVICE_TIMEOUT_*) when one of
+    its bounded internal waits expires.  ``arm()`` queues a 4-byte copy of the
+    word to pinned host memory after a launch; ``poll()`` (cheap, no sync)
+    raises if a completed copy shows an error; ``check()`` synchronizes.
+    """
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.word = torch.zeros(1, dtype=torch.int32, device=device)
+        self.host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.event = None
+
+    @property
+    def ptr(self) -> int:
+        return self.word.data_ptr()
+
+    def arm(self):
+        self.host.copy_(self.word, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record(torch.cuda.current_stream(self.device))
+
+    def poll(self):
+        if self.event is not None and self.event.query():
+            self._raise_if_set(int(self.host.item()))
+
+    def check(self):
+        torch.cuda.current_stream(self.device).synchronize()
+        self._raise_if_set(int(self.word.item()))
+
+    def _raise_if_set(self, code: int):
+        if code:
+            self.word.zero_()
+            self.host.zero_()
+            raise RuntimeError(f"b200 attention kernel aborted: bounded wait expired (device status {code})")
+
+
+def _check16(t: torch.Tensor, what: str):
+    _lib.require_cuda(t, what)
+    if t.dtype not in (torch.bfloat16, torch.float16):
+        raise _lib.UnsupportedAttention(f"{what}: bf16/fp16 required, got {t.dtype}")
+
+
+def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: float = 1e-6,
+            norm_rope: bool = True):
+    """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
+
+    x_*: [n_local, H*D] (row stride may exceed H*D); w_*: [H*D]; freqs:
+    [n_local, D/2, 2, 2] fp32 (ignored when norm_rope is False).
+    """
+    lib = _lib.load()
+    for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v"), (send, "send")):
+        _check16(t, f"prepass {name}")
+    n = geo.n_local
+    width = geo.heads * geo.head_dim
+    for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v")):
+        if t.dim() != 2 or t.shape[0] != n or t.shape[1] != width or t.stride(1) != 1:
+            raise ValueError(f"prepass {name}: expected [{n}, {width}] with unit inner stride, got "
+                             f"{tuple(t.shape)} / {t.stride()}")
+        if t.dtype != send.dtype:
+            raise ValueError("prepass: q/k/v and send dtypes differ")
+    if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
+        raise ValueError(f"prepass: send must be contiguous {geo.send_shape()}")
+    w_dtype = _lib.dtype_code(send.dtype)
+    fptr, fstride = 0, 0
+    wq = wk = 0
+    if norm_rope:
+        for t, name in ((w_q, "w_q"), (w_k, "w_k")):
+            if t.dim() != 1 or t.shape[0] != width or not t.is_contiguous() or t.device != send.device:
+                raise ValueError(f"prepass {name}: expected contiguous [{width}] on {send.device}")
+        if w_q.dtype != w_k.dtype:
+            raise ValueError("prepass: norm weights must share a dtype")
+        w_dtype = _lib.dtype_code(w_q.dtype)
+        wq, wk = w_q.data_ptr(), w_k.data_ptr()
+        if freqs.dtype != torch.float32 or freqs.device != send.device:
+            raise ValueError("prepass: freqs must be fp32 on the send device")
+        if (freqs.dim() != 4 or freqs.shape[0] != n or tuple(freqs.shape[1:]) != (geo.head_dim // 2, 2, 2)
+                or freqs.stride()[1:] != (4, 2, 1) or freqs.stride(0) % 4 != 0):
+            raise ValueError(f"prepass: freqs must be [{n}, {geo.head_dim // 2}, 2, 2] with contiguous rows")
+        fptr, fstride = freqs.data_ptr(), freqs.stride(0)
+    rc = lib.ps_b200_prepass(
+        x_q.data_ptr(), x_k.data_ptr(), x_v.data_ptr(),
+        _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]),
+        wq, wk, w_dtype, fptr, fstride, send.data_ptr(), _lib.dtype_code(send.dtype),
+        geo.world, n, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
+        1 if norm_rope else 0, _lib.stream_handle(send.device))
+    _lib.check(rc, "ps_b200_prepass")
+
+
+def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status: DeviceStatus | None):
+    """Attention over the receive buffer [W,3,width,h,D] for this rank's real heads."""
+    lib = _lib.load()
+    _check16(recv, "attention recv")
+    _lib.require_cuda(out_send, "attention out")
+    if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
+        raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")
+    if tuple(out_send.shape) != geo.out_shape() or not out_send.is_contiguous():
+        raise ValueError(f"attention: out must be contiguous {geo.out_shape()}")
+    if out_send.dtype not in (recv.dtype, torch.float32):
+        raise ValueError("attention: output dtype must be fp32 or the input dtype")
+    rc = lib.ps_b200_ulysses_attn_fwd(
+        recv.data_ptr(), out_send.data_ptr(), _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype),
+        geo.world, geo.width, geo.total, geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale),
+        status.ptr if status is not None else None, _lib.stream_handle(recv.device))
+    _lib.check(rc, "ps_b200_ulysses_attn_fwd")
+    if status is not None:
+        status.arm()
+
+
+def unpack(out_recv, out, geo: UlyssesGeometry):
+    """[W,width,h,D] received outputs -> out [n_local, H, D] (real heads only)."""
+    lib = _lib.load()
+    _check16(out_recv, "unpack recv")
+    _lib.require_cuda(out, "unpack out")
+    if tuple(out_recv.shape) != geo.out_shape() or not out_recv.is_contiguous():
+        raise ValueError(f"unpack: recv must be contiguous {geo.out_shape()}")
+    if (out.dim() != 3 or tuple(out.shape) != (geo.n_local, geo.heads, geo.head_dim)
+            or out.stride(2) != 1 or out.stride(1) != geo.head_dim):
+        raise ValueError(f"unpack: out must be [{geo.n_local}, {geo.heads}, {geo.head_dim}] with packed heads")
+    rc = lib.ps_b200_unpack(
+        out_recv.data_ptr(), out.data_ptr(), out.stride(0), _lib.dtype_code(out_recv.dtype),
+        _lib.dtype_code(out.dtype), geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank,
+        geo.head_dim, _lib.stream_handle(out.device))
+    _lib.check(rc, "ps_b200_unpack")
+
+
+def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None):
+    """softmax(Q K^T * scale) V for BLHD tensors (GQA by head grouping)."""
+    lib = _lib.load()
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _check16(t, f"attention {name}")
+        if t.stride(3) != 1:
+            raise ValueError(f"attention {name}: head_dim must be contiguous")
+    _lib.require_cuda(out, "attention out")
+    b, lq, hq, d = q.shape
+    lk, hk = k.shape[1], k.shape[2]
+
+    def st(t):  # {batch, segment, row, head}; one segment spanning the sequence
+        return _lib.i64([t.stride(0), t.stride(0), t.stride(1), t.stride(2)])
+
+    rc = lib.ps_b200_attn_fwd(
+        q.data_ptr(), st(q), k.data_ptr(), st(k), v.data_ptr(), st(v), out.data_ptr(), st(out),
+        _lib.dtype_code(q.dtype), _lib.dtype_code(out.dtype), b, hq, hk, d,
+        lq, 1, lq, lk, 1, lk, float(scale), status.ptr if status is not None else None,
+        _lib.stream_handle(q.device))
+    _lib.check(rc, "ps_b200_attn_fwd")
+    if status is not None:
+        status.arm()

@@ -1,0 +1,113 @@
+"""Ulysses sequence-parallel self-attention of one block on this rank.
+
+Data path (one process per GPU, NCCL through torch.distributed):
+
+  pre-pass kernel   q/k RMSNorm + RoPE, written straight into the send buffer
+                    send [W][3][width][h][D] (bf16)
+  all_to_all_single send -> recv (skipped when W == 1: recv is send)
+  attention kernel  reads recv in place (one key/value segment per source
+                    rank) for this rank's h heads, writes the output send
+                    buffer [W][width][h][D] - or, when W == 1, the final
+                    [n][H][D] output directly
+  all_to_all_single out_send -> out_recv
+  unpack kernel     out_recv -> [n][H][D], dropping padded heads
+
+This replaces, for one batch row, powershard/wan_model.py:421-430
+(attention_qkv) + 343-364 (ulysses_to_sequence) + 398-418 (run_attention) +
+367-381 (ulysses_to_heads).  Buffers are cached per (device, stream,
+geometry, dtype) and reused; the returned output is always a fresh tensor.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .partition import UlyssesGeometry
+
+
+class UlyssesAttention:
+    """Per-rank engine; `group` is the sequence-parallel process group."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self._buffers = {}
+        self._status = {}
+
+    # ------------------------------------------------------------ topology
+    def world_rank(self):
+        if dist.is_available() and dist.is_initialized():
+            return dist.get_world_size(self.group), dist.get_rank(self.group)
+        return 1, 0
+
+    def geometry(self, total: int, heads: int, head_dim: int, local: bool = False) -> UlyssesGeometry:
+        world, rank = (1, 0) if local else self.world_rank()
+        return UlyssesGeometry(total=total, heads=heads, head_dim=head_dim, world=world, rank=rank)
+
+    # ------------------------------------------------------------ buffers
+    def _workspace(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (device.index, stream, geo.world, geo.width, geo.heads_per_rank, geo.head_dim, dtype)
+        ws = self._buffers.get(key)
+        if ws is None:
+            send = torch.empty(geo.send_shape(), dtype=dtype, device=device)
+            recv = send if geo.world == 1 else torch.empty_like(send)
+            out_send = None if geo.world == 1 else torch.empty(geo.out_shape(), dtype=dtype, device=device)
+            out_recv = None if geo.world == 1 else torch.empty_like(out_send)
+            ws = dict(send=send, recv=recv, out_send=out_send, out_recv=out_recv)
+            self._buffers[key] = ws
+        if device.index not in self._status:
+            self._status[device.index] = ops.DeviceStatus(device)
+        return ws, self._status[device.index]
+
+    def _exchange(self, recv, send, geo):
+        if geo.world > 1:
+            dist.all_to_all_single(recv, send, group=self.group)
+
+    # ------------------------------------------------------------ forward
+    def forward(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
+                eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
+                norm_rope: bool = True, state: dict | None = None, local: bool = False) -> torch.Tensor:
+        """One block's self-attention for this rank's tokens.
+
+        x_q/x_k/x_v: [n_local, H*D] q/k/v projection outputs (bf16/fp16).
+        With norm_rope, w_q/w_k [H*D] are the RMSNorm weights and freqs is
+        the rank's rotation table [n_local, D/2, 2, 2] fp32; without it the
+        inputs are already normalised/rotated and are only exchanged.
+        Returns [n_local, H, D] in out_dtype (default: the input dtype).
+        local=True runs the block on this rank alone (no exchange, W = 1).
+        """
+        device = x_q.device
+        dtype = x_q.dtype
+        head_dim = x_q.shape[-1] // heads
+        geo = self.geometry(total, heads, head_dim, local)
+        if x_q.shape[0] != geo.n_local:
+            raise ValueError("Ulysses local token/head geometry mismatch")
+        out_dtype = out_dtype or dtype
+        scale = head_dim ** -0.5 if scale is None else float(scale)
+        with torch.cuda.device(device):
+            ws, status = self._workspace(geo, dtype, device)
+            status.poll()
+            out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
+            ops.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope)
+            self._exchange(ws["recv"], ws["send"], geo)
+            if geo.world == 1:
+                ops.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status)
+            else:
+                ops.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status)
+                self._exchange(ws["out_recv"], ws["out_send"], geo)
+                ops.unpack(ws["out_recv"], out, geo)
+        if state is not None:
+            qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+            state["padded_heads"] = geo.padded_heads
+            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
+            state["out_collectives"] = state.get("out_collectives", 0) + 1
+            state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
+            state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
+        return out
+
+    def check(self):
+        """Synchronize and raise if any attention launch aborted on the device."""
+        for status in self._status.values():
+            status.check()

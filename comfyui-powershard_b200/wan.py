@@ -1,0 +1,126 @@
+"""Wan self-attention entry points with the PowerShard signatures.
+
+* ``self_attention_forward(self, x, freqs, transformer_options=None)`` -
+  replacement for powershard/wan_model.py:433-438.  Projections stay torch
+  Linear layers; q/k RMSNorm + RoPE run fused with the Ulysses pack in one
+  kernel, attention and unpack in the b200 kernels.
+* ``sequence_attention(self, q, k, v, total=None)`` - replacement for
+  powershard/wan_model.py:441-502 for callers that already produced
+  normalised, rotated q/k (the pre-pass then only packs).
+
+Both read the module attributes the reference installs
+(``install_wan_compute``, wan_model.py:727-768): ``num_heads``,
+``head_dim``, ``_ps_sequence`` (the shared state dict: ``enabled``,
+``ulysses``, ``total`` ...), and update the same counters
+(``kv_collectives``, ``kv_gathered_bytes``, ``out_collectives``,
+``out_exchanged_bytes``, ``padded_heads``, ``effective_comm_dtype``).
+The sequence-parallel process group is ``_ps_b200_group`` (None = default).
+"""
+from __future__ import annotations
+
+import types
+
+import torch
+
+from .contract import AttentionOptions, UnsupportedAttention
+from .ulysses import UlyssesAttention
+
+WIRE_DTYPE = torch.bfloat16
+
+
+def _engine(module) -> UlyssesAttention:
+    engine = getattr(module, "_ps_b200_engine", None)
+    if engine is None:
+        engine = UlyssesAttention(getattr(module, "_ps_b200_group", None))
+        module._ps_b200_engine = engine
+    return engine
+
+
+def _state(module) -> dict:
+    state = getattr(module, "_ps_sequence", None)
+    if state is None:
+        state = dict(total=0, enabled=False, ulysses=True, comm_dtype="bf16", mode="ulysses")
+        module._ps_sequence = state
+    return state
+
+
+def _check_supported(module, state):
+    if state.get("enabled") and not state.get("ulysses", True):
+        raise UnsupportedAttention("b200: token mode (K/V all-gather) is not provided; use sequence_mode='ulysses'")
+    if getattr(module, "_ps_main", False) and state.get("ref_attn_masks") is not None:
+        raise UnsupportedAttention("b200: InfiniteTalk reference attention maps are not provided")
+
+
+def _rows(t, heads, head_dim, dtype):
+    """[n, H, D] or [n, H*D] -> contiguous [n, H*D] in the wire dtype."""
+    t = t.reshape(t.shape[0], heads * head_dim)
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    if t.stride(1) != 1 or t.stride(0) % 8 or t.data_ptr() % 16:
+        t = t.contiguous()
+    return t
+
+
+def self_attention_forward(self, x, freqs, transformer_options=None):
+    """x [B, n, dim] -> [B, n, dim] through the fused Ulysses path."""
+    state = _state(self)
+    _check_supported(self, state)
+    batch, n, _ = x.shape
+    heads, dim = self.num_heads, self.head_dim
+    total = state["total"] if state.get("enabled") else n
+    engine = _engine(self)
+    table = freqs[0, :, 0]
+    if table.dtype != torch.float32 or table.stride()[1:] != (4, 2, 1) or table.data_ptr() % 16:
+        table = table.float().contiguous()
+    w_q = self.norm_q.weight
+    w_k = self.norm_k.weight
+    if w_q.dtype not in (torch.float32, WIRE_DTYPE):
+        w_q, w_k = w_q.float(), w_k.float()
+    eps = self.norm_q.eps if self.norm_q.eps is not None else 1e-6
+    q_lin, k_lin, v_lin = self.q(x), self.k(x), self.v(x)
+    outs = []
+    for b in range(batch):
+        outs.append(engine.forward(
+            _rows(q_lin[b], heads, dim, WIRE_DTYPE), _rows(k_lin[b], heads, dim, WIRE_DTYPE),
+            _rows(v_lin[b], heads, dim, WIRE_DTYPE), w_q.contiguous(), w_k.contiguous(), table,
+            total=total, heads=heads, eps=eps, norm_rope=True, local=not state.get("enabled"),
+            state=state if (b == 0 and state.get("enabled")) else None))
+    out = torch.stack(outs)
+    return self.o(out.reshape(batch, n, heads * dim).to(x.dtype if x.is_floating_point() else out.dtype))
+
+
+def sequence_attention(self, q, k, v, total=None):
+    """q, k, v [B, n, H, D] (already RMSNorm'd and rotated) -> [B, n, H, D] fp32."""
+    state = _state(self)
+    _check_supported(self, state)
+    batch, n, heads, dim = q.shape
+    if not state.get("enabled"):
+        from .provider import B200Provider
+        provider = getattr(self, "_ps_b200_provider", None) or B200Provider()
+        self._ps_b200_provider = provider
+        out = provider(q.to(WIRE_DTYPE), k.to(WIRE_DTYPE), v.to(WIRE_DTYPE),
+                       AttentionOptions(softmax_scale=dim ** -0.5))
+        return out.float()
+    total = total or state["total"]
+    engine = _engine(self)
+    outs = []
+    for b in range(batch):
+        outs.append(engine.forward(
+            _rows(q[b], heads, dim, WIRE_DTYPE), _rows(k[b], heads, dim, WIRE_DTYPE),
+            _rows(v[b], heads, dim, WIRE_DTYPE), total=total, heads=heads, norm_rope=False,
+            out_dtype=torch.float32, state=state if b == 0 else None))
+    return torch.stack(outs)
+
+
+def install_self_attention(module, group=None, state: dict | None = None):
+    """Route one WanSelfAttention-like module through the b200 path.
+
+    The counterpart of the ``"self"`` branch of install_wan_compute
+    (powershard/wan_model.py:740-746): replaces ``module.forward`` and
+    attaches the shared sequence state and process group.
+    """
+    module.forward = types.MethodType(self_attention_forward, module)
+    module._ps_b200_group = group
+    if state is not None:
+        module._ps_sequence = state
+    return module

@@ -1,0 +1,123 @@
+/*
+ * ps_b200.h - C ABI of the B200 (sm_100a) Ulysses sequence-parallel attention
+ * provider for ComfyUI-PowerShard.
+ *
+ * The library (libps_b200.so) holds hand-written CUDA kernels for the three
+ * device steps of PowerShard's Ulysses self-attention block; the all-to-all
+ * exchanges between them are issued by the host (NCCL through
+ * torch.distributed).  Every entry point takes plain device pointers, sizes
+ * and a cudaStream_t (as void*), launches asynchronously on that stream and
+ * returns a status code; no entry point allocates device memory.
+ *
+ * Reference interfaces replaced (paths inside the ComfyUI-PowerShard tree):
+ *   ps_b200_prepass        powershard/wan_model.py:421-430 (attention_qkv:
+ *                          norm_q/norm_k RMSNorm + rope_apply) fused with the
+ *                          send-side packing of ulysses_to_sequence,
+ *                          wan_model.py:343-361 / attention.py:57-75.
+ *   ps_b200_attn_fwd       the provider call of AttentionDispatcher.__call__,
+ *                          powershard/attention_policy.py:101-149 (semantics of
+ *                          attention_contract.py:85-145, non-causal, no mask).
+ *   ps_b200_ulysses_attn_fwd  the same attention reading the receive buffer of
+ *                          ulysses_to_sequence in place (wan_model.py:362-364)
+ *                          and writing the send buffer of ulysses_to_heads
+ *                          (wan_model.py:373-376).
+ *   ps_b200_unpack         receive-side unpack of ulysses_to_heads,
+ *                          powershard/wan_model.py:377-380 / attention.py:93-95.
+ *
+ * Layout vocabulary: a "segmented" tensor is [batch][segment][row][head][d]
+ * with arbitrary element strides for the first four axes and d contiguous.
+ * Rows of segment s are valid while s*seg_rows + row < len; the Ulysses
+ * receive buffer is one segment per source rank.
+ */
+#ifndef PS_B200_H
+#define PS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PS_B200_ABI_VERSION 1
+
+/* Return codes. */
+#define PS_B200_OK 0
+#define PS_B200_ERR_INVALID 1     /* bad pointer / size / stride / alignment      */
+#define PS_B200_ERR_UNSUPPORTED 2 /* valid request outside what the kernels cover */
+#define PS_B200_ERR_CUDA 3        /* CUDA runtime or driver error                  */
+
+/* Element types. */
+#define PS_B200_BF16 0
+#define PS_B200_FP16 1
+#define PS_B200_FP32 2
+
+/* Device status codes written to *status by the attention kernel when one of
+ * its bounded internal waits expires (the launch then returns early, the
+ * output is undefined and the host must raise).  0 means success. */
+#define PS_B200_DEVICE_TIMEOUT_FIRST 101
+#define PS_B200_DEVICE_TIMEOUT_LAST 199
+
+/* ABI version of the loaded library (PS_B200_ABI_VERSION). */
+int ps_b200_abi_version(void);
+
+/* Message of the last error returned on the calling host thread. */
+const char* ps_b200_last_error(void);
+
+/*
+ * Fused q/k RMSNorm + RoPE + Ulysses pack (replaces attention_qkv plus the
+ * send-side packing of ulysses_to_sequence).
+ *   x_q, x_k, x_v  [n_local][heads*head_dim] projection outputs (dtype), row
+ *                  strides x_row_strides[0..2] in elements (16-byte aligned).
+ *   w_qnorm, w_knorm [heads*head_dim] RMSNorm weights, w_dtype = dtype or FP32.
+ *   freqs          [n_local][head_dim/2][2][2] fp32 rotation table (the
+ *                  reference's freqs[0, :, 0]), freqs_row_stride in floats.
+ *   send           [world][3][seg_rows][heads_per_rank][head_dim] (dtype).
+ *   norm_rope      1: RMSNorm + RoPE on q and k (Wan self-attention),
+ *                  0: pack only.
+ * Rows n_local..seg_rows-1 and heads heads..world*heads_per_rank-1 of the
+ * send buffer are written as zeros.
+ */
+int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                    const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,
+                    int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
+                    int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream);
+
+/*
+ * softmax(Q K^T * softmax_scale) V over segmented tensors (BLHD is the case
+ * segs = 1, seg_rows = len).  q/k/v/out strides are {batch, segment, row,
+ * head} in elements; all must be multiples of 8 elements and pointers 16-byte
+ * aligned.  dtype BF16 or FP16 for q/k/v, out_dtype = dtype or FP32; head_dim 128;
+ * heads_q % heads_kv == 0 (GQA).  status: device int (may be NULL) that
+ * receives a PS_B200_DEVICE_TIMEOUT_* code if the kernel aborts.
+ */
+int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                     const void* v, const int64_t v_strides[4], void* out, const int64_t out_strides[4],
+                     int dtype, int out_dtype, int batch, int heads_q, int heads_kv, int head_dim, int seg_rows_q,
+                     int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k, float softmax_scale,
+                     int* status, void* stream);
+
+/*
+ * Attention over the Ulysses receive buffer recv [world][3][seg_rows][heads_per_rank][head_dim]
+ * for heads 0..heads_valid-1 of this rank, sequence length `total`; the
+ * result goes to out_send [world][seg_rows][heads_per_rank][head_dim], the
+ * send buffer of the inverse all-to-all (rows >= the destination's valid
+ * rows and heads >= heads_valid are left untouched).  out_dtype = dtype or
+ * FP32 (then out_send holds fp32 elements).
+ */
+int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
+                             int total, int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
+                             int* status, void* stream);
+
+/*
+ * Inverse unpack: recv [world][seg_rows][heads_per_rank][head_dim] (dtype)
+ * -> out [n_local][heads][head_dim] (out_dtype = dtype or FP32), token row
+ * stride out_row_stride elements.  Padded heads are dropped.
+ */
+int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
+                   int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PS_B200_H */

@@ -1,0 +1,218 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run once in a container that has the ComfyUI-PowerShard source tree
+(default ``/root/reference``; override with POWERSHARD_REFERENCE):
+
+    python tests/golden/make_golden.py
+
+It imports the reference package from that tree (torch only, no ComfyUI),
+runs the reference's own hot-path functions on seeded inputs and saves
+inputs + outputs with torch.save next to this script:
+
+* ``attention_qkv.pt``  - operations.RMSNorm + wan_model.rope_apply through
+  wan_model.attention_qkv (fp32 and bf16 projections).
+* ``ulysses_exchange.pt`` - attention.ulysses_heads_to_sequence ->
+  math_attention -> ulysses_sequence_to_heads for W in {3,4,5,6}, heads 7 and
+  56, 2W+1 tokens, D=8, V*1e6 (the geometry of the reference's own
+  tests/test_sequence_distributed.py), plus wan_model.ulysses_to_sequence /
+  ulysses_to_heads at D=128.
+* ``math_attention.pt`` - attention_contract.math_attention cases.
+* ``sequence_attention.pt`` - wan_model.sequence_attention (Ulysses, math
+  provider, fp32 wire) for W in {1,2,3} on a 40-token, 5-head, D=128 layer.
+
+Collectives are emulated in-process with one thread per rank (the same
+technique as the reference's test_ulysses_tensor_permutation_reference).
+"""
+from __future__ import annotations
+
+import os
+import sys
+import threading
+from concurrent.futures import ThreadPoolExecutor
+from contextlib import contextmanager
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+import torch.distributed as dist
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("POWERSHARD_REFERENCE", "/root/reference"))
+
+
+@contextmanager
+def emulated_collectives(world):
+    """Patch torch.distributed with a thread-per-rank in-process transport."""
+    local = threading.local()
+    barrier = threading.Barrier(world, timeout=60)
+    slots = [None] * world
+    saved = {n: getattr(dist, n) for n in ("get_world_size", "get_rank", "all_to_all_single",
+                                           "all_gather_into_tensor", "all_reduce")}
+
+    def all_to_all(output, input, group=None):
+        slots[local.rank] = input.clone()
+        barrier.wait()
+        output.copy_(torch.stack([slots[r][local.rank] for r in range(world)]))
+        barrier.wait()
+
+    def all_gather(output, input, group=None):
+        slots[local.rank] = input.clone()
+        barrier.wait()
+        output.copy_(torch.cat(slots))
+        barrier.wait()
+
+    def all_reduce(value, op=None, group=None):
+        slots[local.rank] = value.clone()
+        barrier.wait()
+        value.copy_(torch.stack(slots).amax(0))
+        barrier.wait()
+
+    dist.get_world_size = lambda group=None: world
+    dist.get_rank = lambda group=None: local.rank
+    dist.all_to_all_single = all_to_all
+    dist.all_gather_into_tensor = all_gather
+    dist.all_reduce = all_reduce
+
+    def run(fn):
+        def worker(rank):
+            local.rank = rank
+            try:
+                return fn(rank)
+            except BaseException:
+                barrier.abort()
+                raise
+        with ThreadPoolExecutor(max_workers=world) as ex:
+            return list(ex.map(worker, range(world)))
+    try:
+        yield run
+    finally:
+        for n, f in saved.items():
+            setattr(dist, n, f)
+
+
+def rope_table(n, pairs, seed):
+    g = torch.Generator().manual_seed(seed)
+    ang = torch.rand(n, pairs, generator=g, dtype=torch.float64) * 40.0
+    c, s = torch.cos(ang), torch.sin(ang)
+    return torch.stack([c, -s, s, c], -1).reshape(1, n, 1, pairs, 2, 2).float()
+
+
+def main():
+    sys.path.insert(0, str(REF))
+    torch.set_num_threads(4)
+    from powershard import wan_model, attention
+    from powershard.attention_contract import AttentionOptions, math_attention
+    from powershard.attention_policy import AttentionDispatcher
+    from powershard.config import DistributedConfig, shard_bounds
+    from powershard.operations import RMSNorm
+
+    # ---------------------------------------------------------- attention_qkv
+    cases = []
+    for dtype in (torch.float32, torch.bfloat16):
+        g = torch.Generator().manual_seed(11)
+        n, heads, dim = 37, 3, 128
+        q_lin, k_lin, v_lin = (torch.randn(1, n, heads * dim, generator=g).to(dtype) * 1.7 for _ in range(3))
+        wq = (torch.rand(heads * dim, generator=g) + 0.5).to(dtype)
+        wk = (torch.rand(heads * dim, generator=g) + 0.5).to(dtype)
+        freqs = rope_table(n, dim // 2, 5)
+        norm_q, norm_k = RMSNorm(heads * dim, eps=1e-6, dtype=dtype), RMSNorm(heads * dim, eps=1e-6, dtype=dtype)
+        norm_q.weight.data.copy_(wq)
+        norm_k.weight.data.copy_(wk)
+        mod = SimpleNamespace(num_heads=heads, head_dim=dim, norm_q=norm_q, norm_k=norm_k,
+                              q=lambda x, t=q_lin: t, k=lambda x, t=k_lin: t, v=lambda x, t=v_lin: t)
+        with torch.no_grad():
+            q, k, v = wan_model.attention_qkv(mod, torch.zeros(1, n, heads * dim), freqs)
+        cases.append(dict(dtype=str(dtype), heads=heads, eps=1e-6, q_lin=q_lin, k_lin=k_lin, v_lin=v_lin,
+                          wq=wq, wk=wk, freqs=freqs, q=q, k=k, v=v))
+    torch.save(cases, HERE / "attention_qkv.pt")
+
+    # ------------------------------------------------------ Ulysses exchange
+    exchange = []
+    for world in (3, 4, 5, 6):
+        for heads in (7, 56):
+            total, dim = 2 * world + 1, 8
+            gen = torch.Generator().manual_seed(991)
+            q, k = (torch.randn(total, heads, dim, generator=gen) for _ in range(2))
+            v = torch.randn(total, heads, dim, generator=gen) * 1e6
+
+            def rank_fn(rank):
+                a, b = shard_bounds(total, rank, world)
+                (qg, kg, vg), padded, nbytes = attention.ulysses_heads_to_sequence(
+                    (q[a:b], k[a:b], v[a:b]), total, heads)
+                got = math_attention(qg[None], kg[None], vg[None], AttentionOptions(), 3, 5)[0]
+                local = attention.ulysses_sequence_to_heads(got, total, heads)
+                return dict(qg=qg, kg=kg, vg=vg, padded=padded, nbytes=nbytes, attn=got, out=local)
+            with emulated_collectives(world) as run:
+                per_rank = run(rank_fn)
+            exchange.append(dict(layout="LHD", world=world, heads=heads, total=total, dim=dim,
+                                 q=q, k=k, v=v, ranks=per_rank))
+    # Batch-first Wan helpers at D=128, uneven heads and tokens.
+    for world in (2, 3):
+        total, heads, dim = 2 * world + 3, 5, 128
+        gen = torch.Generator().manual_seed(17)
+        q, k, v = (torch.randn(1, total, heads, dim, generator=gen) for _ in range(3))
+
+        def rank_fn(rank):
+            a, b = shard_bounds(total, rank, world)
+            (qg, kg, vg), padded, nbytes = wan_model.ulysses_to_sequence(
+                (q[:, a:b], k[:, a:b], v[:, a:b]), total, heads)
+            back, nbytes_out = wan_model.ulysses_to_heads(qg, total, heads)
+            return dict(qg=qg, kg=kg, vg=vg, padded=padded, nbytes=nbytes, back=back, nbytes_out=nbytes_out)
+        with emulated_collectives(world) as run:
+            per_rank = run(rank_fn)
+        exchange.append(dict(layout="BLHD", world=world, heads=heads, total=total, dim=dim,
+                             q=q, k=k, v=v, ranks=per_rank))
+    torch.save(exchange, HERE / "ulysses_exchange.pt")
+
+    # --------------------------------------------------------- math_attention
+    mcases = []
+    g = torch.Generator().manual_seed(9)
+    for (b, lq, lk, h, scale, qc, kc) in ((2, 5, 7, 4, .13, 2, 3), (2, 5, 7, 4, .37, 128, 512),
+                                          (1, 300, 300, 2, None, 128, 512), (1, 129, 513, 1, .09, 128, 512)):
+        q = torch.randn(b, lq, h, 128, generator=g)
+        k = torch.randn(b, lk, h, 128, generator=g)
+        v = torch.randn(b, lk, h, 128, generator=g)
+        out = math_attention(q, k, v, AttentionOptions(softmax_scale=scale), qc, kc)
+        mcases.append(dict(q=q, k=k, v=v, scale=scale, query_chunk=qc, key_chunk=kc, out=out))
+    torch.save(mcases, HERE / "math_attention.pt")
+
+    # ------------------------------------------------------ sequence_attention
+    scases = []
+    n_total, heads, dim = 40, 5, 128
+    g = torch.Generator().manual_seed(23)
+    q_lin, k_lin, v_lin = (torch.randn(1, n_total, heads * dim, generator=g) for _ in range(3))
+    wq = torch.rand(heads * dim, generator=g) + 0.5
+    wk = torch.rand(heads * dim, generator=g) + 0.5
+    freqs = rope_table(n_total, dim // 2, 3)
+    for world in (1, 2, 3):
+        cfg = DistributedConfig(attention_backend="math", sequence_mode="ulysses")
+
+        def rank_fn(rank):
+            a, b = shard_bounds(n_total, rank, world)
+            norm_q, norm_k = RMSNorm(heads * dim, eps=1e-6), RMSNorm(heads * dim, eps=1e-6)
+            norm_q.weight.data.copy_(wq)
+            norm_k.weight.data.copy_(wk)
+            state = wan_model.new_sequence_state(cfg)
+            state.update(total=n_total, enabled=True, kv_collectives=0, kv_gathered_bytes=0, out_collectives=0,
+                         out_exchanged_bytes=0, padded_heads=0, scale_collectives=0)
+            mod = SimpleNamespace(num_heads=heads, head_dim=dim, norm_q=norm_q, norm_k=norm_k,
+                                  q=lambda x: q_lin[:, a:b], k=lambda x: k_lin[:, a:b], v=lambda x: v_lin[:, a:b],
+                                  _ps_qk_scales=(1., 1., 1.), _ps_sequence=state,
+                                  _ps_attention=AttentionDispatcher(cfg), _ps_group="wan_self", _ps_safe=False)
+            with torch.no_grad():
+                q, k, v = wan_model.attention_qkv(mod, torch.zeros(1, b - a, heads * dim), freqs[:, a:b])
+                out = wan_model.sequence_attention(mod, q, k, v)
+            counters = {key: state[key] for key in ("kv_collectives", "kv_gathered_bytes", "out_collectives",
+                                                    "out_exchanged_bytes", "padded_heads", "effective_comm_dtype")}
+            return dict(bounds=(a, b), out=out, counters=counters)
+        with emulated_collectives(world) as run:
+            per_rank = run(rank_fn)
+        scases.append(dict(world=world, heads=heads, total=n_total, dim=dim, ranks=per_rank))
+    torch.save(dict(q_lin=q_lin, k_lin=k_lin, v_lin=v_lin, wq=wq, wk=wk, freqs=freqs, eps=1e-6,
+                    cases=scases), HERE / "sequence_attention.pt")
+    sizes = {p.name: p.stat().st_size for p in HERE.glob("*.pt")}
+    print("wrote", sizes)
+
+
+if __name__ == "__main__":
+    main()

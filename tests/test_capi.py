@@ -1,0 +1,91 @@
+"""The C ABI library: it loads, exports every symbol include/ps_b200.h
+declares, and rejects invalid or unsupported requests with the documented
+codes before touching the GPU (these calls need no device)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "ps_b200.h").read_text()
+    return sorted(set(re.findall(r"\b(ps_b200_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from powershard_b200 import _lib, build_lib
+    build_lib.build()
+    return _lib.load()
+
+
+def test_exports_every_header_symbol(lib):
+    from powershard_b200 import _lib
+    names = header_symbols()
+    assert names, "no ps_b200_* declarations found in the header"
+    for name in names:
+        assert hasattr(lib, name), f"{name} not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_abi_version(lib):
+    assert lib.ps_b200_abi_version() == 1
+
+
+def test_unsupported_dtype_is_reported_before_launch(lib):
+    from powershard_b200 import _lib
+    strides = _lib.i64([0, 0, 0])
+    rc = lib.ps_b200_prepass(None, None, None, strides, None, None, 0, None, 0, None, _lib.FP32,
+                             1, 0, 0, 1, 1, 128, 1e-6, 1, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    assert b"bf16" in lib.ps_b200_last_error()
+
+
+def test_unsupported_head_dim(lib):
+    from powershard_b200 import _lib
+    st = _lib.i64([0, 0, 128, 64])
+    rc = lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 64,
+                              4, 1, 4, 4, 1, 4, 0.1, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    assert b"head_dim" in lib.ps_b200_last_error()
+
+
+def test_invalid_geometry(lib):
+    from powershard_b200 import _lib
+    # heads_per_rank * world < heads
+    rc = lib.ps_b200_unpack(16, 16, 128, _lib.BF16, _lib.BF16, 2, 1, 1, 5, 2, 128, None)
+    assert rc == _lib.ERR_INVALID
+    # empty key set with queries
+    st = _lib.i64([0, 0, 128, 128])
+    rc = lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
+                              4, 1, 4, 4, 1, 0, 0.1, None, None)
+    assert rc == _lib.ERR_INVALID
+    # misaligned pointer
+    rc = lib.ps_b200_attn_fwd(18, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
+                              4, 1, 4, 4, 1, 4, 0.1, None, None)
+    assert rc == _lib.ERR_INVALID
+    assert b"aligned" in lib.ps_b200_last_error()
+
+
+def test_empty_work_is_a_no_op(lib):
+    from powershard_b200 import _lib
+    st = _lib.i64([0, 0, 128, 128])
+    assert lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
+                                4, 1, 0, 4, 1, 4, 0.1, None, None) == _lib.OK
+    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 2, 3, 0, 2, 2, 128, 0.1, None, None) == _lib.OK
+
+
+def test_error_mapping_to_reference_exceptions():
+    from powershard_b200 import _lib
+    from powershard_b200.contract import UnsupportedAttention
+    lib = _lib.load()
+    rc = lib.ps_b200_unpack(16, 16, 128, _lib.FP32, _lib.FP32, 1, 1, 1, 1, 1, 128, None)
+    with pytest.raises(UnsupportedAttention):
+        _lib.check(rc, "unpack")
+    rc = lib.ps_b200_unpack(16, 16, 128, _lib.BF16, _lib.BF16, 2, 1, 1, 5, 2, 128, None)
+    with pytest.raises(ValueError):
+        _lib.check(rc, "unpack")

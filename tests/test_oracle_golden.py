@@ -1,0 +1,126 @@
+"""Pin the CPU oracle to the reference: every oracle function against the
+fixtures recorded from ComfyUI-PowerShard itself (tests/golden/make_golden.py).
+"""
+import pytest
+import torch
+
+
+def load(golden_dir, name):
+    return torch.load(golden_dir / name, weights_only=False)
+
+
+@pytest.mark.parametrize("index", [0, 1])
+def test_attention_qkv_matches_reference(oracle, golden_dir, index):
+    case = load(golden_dir, "attention_qkv.pt")[index]
+    q, k, v = oracle.attention_qkv(case["q_lin"], case["k_lin"], case["v_lin"], case["wq"], case["wk"],
+                                   case["freqs"], case["heads"], case["eps"])
+    # Same operations in the same order as operations.RMSNorm / rope_apply.
+    torch.testing.assert_close(q, case["q"], atol=0, rtol=0)
+    torch.testing.assert_close(k, case["k"], atol=0, rtol=0)
+    torch.testing.assert_close(v, case["v"], atol=0, rtol=0)
+    assert q.dtype == torch.float32 and v.dtype == case["v"].dtype
+
+
+def test_rope_apply_identity_and_norm(oracle):
+    x = torch.randn(1, 6, 2, 128)
+    ident = oracle.rope_table_3d((1, 1, 1), 128).expand(1, 6, 1, 64, 2, 2)
+    torch.testing.assert_close(oracle.rope_apply(x, ident), x)
+    table = oracle.rope_table_3d((2, 1, 3), 128)
+    out = oracle.rope_apply(x, table)
+    torch.testing.assert_close(out.norm(dim=-1), x.norm(dim=-1), rtol=1e-5, atol=1e-5)
+
+
+def test_rope_axes_split(oracle):
+    assert oracle.rope_axes(128) == (44, 42, 42)
+
+
+@pytest.mark.parametrize("index", range(8))
+def test_ulysses_exchange_lhd_matches_reference(oracle, golden_dir, index):
+    case = load(golden_dir, "ulysses_exchange.pt")[index]
+    assert case["layout"] == "LHD"
+    world, total, heads = case["world"], case["total"], case["heads"]
+    sends = []
+    for r in range(world):
+        a, b = oracle.shard_bounds(total, r, world)
+        sends.append(oracle.pack_qkv(case["q"][a:b], case["k"][a:b], case["v"][a:b], total, r, world))
+    recvs = oracle.exchange(sends)
+    attn_outs = []
+    for r in range(world):
+        ref = case["ranks"][r]
+        q, k, v = oracle.unpack_qkv(recvs[r], total)
+        torch.testing.assert_close(q, ref["qg"], atol=0, rtol=0)
+        torch.testing.assert_close(k, ref["kg"], atol=0, rtol=0)
+        torch.testing.assert_close(v, ref["vg"], atol=0, rtol=0)
+        assert ref["padded"] == -(-heads // world) * world
+        assert ref["nbytes"] == sends[r].numel() * sends[r].element_size()
+        got = oracle.math_attention(q[None], k[None], v[None], None, 3, 5)[0]
+        torch.testing.assert_close(got, ref["attn"], atol=1e-6 * float(v.abs().max()), rtol=1e-5)
+        attn_outs.append(oracle.pack_out(got, total, world))
+    back = oracle.exchange(attn_outs)
+    for r in range(world):
+        out = oracle.unpack_out(back[r], total, heads, r, world)
+        torch.testing.assert_close(out, case["ranks"][r]["out"], atol=1e-6 * float(case["v"].abs().max()),
+                                   rtol=1e-5)
+
+
+@pytest.mark.parametrize("index", [8, 9])
+def test_ulysses_exchange_blhd_matches_reference(oracle, golden_dir, index):
+    case = load(golden_dir, "ulysses_exchange.pt")[index]
+    assert case["layout"] == "BLHD"
+    world, total, heads = case["world"], case["total"], case["heads"]
+    sends = []
+    for r in range(world):
+        a, b = oracle.shard_bounds(total, r, world)
+        sends.append(oracle.pack_qkv(case["q"][0, a:b], case["k"][0, a:b], case["v"][0, a:b], total, r, world))
+    recvs = oracle.exchange(sends)
+    outs = []
+    for r in range(world):
+        q, k, v = oracle.unpack_qkv(recvs[r], total)
+        ref = case["ranks"][r]
+        torch.testing.assert_close(q, ref["qg"][0], atol=0, rtol=0)
+        torch.testing.assert_close(v, ref["vg"][0], atol=0, rtol=0)
+        outs.append(oracle.pack_out(q, total, world))
+    back = oracle.exchange(outs)
+    for r in range(world):
+        out = oracle.unpack_out(back[r], total, heads, r, world)
+        torch.testing.assert_close(out, case["ranks"][r]["back"][0], atol=0, rtol=0)
+        assert case["ranks"][r]["nbytes_out"] == outs[r].numel() * outs[r].element_size()
+
+
+@pytest.mark.parametrize("index", range(4))
+def test_math_attention_matches_reference(oracle, golden_dir, index):
+    case = load(golden_dir, "math_attention.pt")[index]
+    got = oracle.math_attention(case["q"], case["k"], case["v"], case["scale"], case["query_chunk"],
+                                case["key_chunk"])
+    # Same tiling and operation order; only BLAS thread partitioning of the
+    # fp32 matmuls may differ from the recording run (last-bit effects).
+    torch.testing.assert_close(got, case["out"], atol=1e-6, rtol=1e-5)
+    # The fp32 SDPA oracle of the north star agrees with the tiled math path.
+    torch.testing.assert_close(oracle.sdpa_fp32(case["q"], case["k"], case["v"], case["scale"]), case["out"],
+                               atol=1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("index", range(3))
+def test_sequence_attention_matches_reference(oracle, golden_dir, index):
+    data = load(golden_dir, "sequence_attention.pt")
+    case = data["cases"][index]
+    outs = oracle.sequence_attention(data["q_lin"], data["k_lin"], data["v_lin"], data["wq"], data["wk"],
+                                     data["freqs"], case["heads"], case["world"], data["eps"],
+                                     wire_dtype=torch.float32, attention="math", provider_dtype=torch.float16)
+    for r, ref in enumerate(case["ranks"]):
+        torch.testing.assert_close(outs[r], ref["out"], atol=1e-6, rtol=1e-5)
+        assert ref["counters"]["kv_collectives"] == 1 and ref["counters"]["out_collectives"] == 1
+
+
+def test_sdpa_oracle_close_to_reference_path(oracle, golden_dir):
+    """The fp32 SDPA oracle used for CUDA parity differs from the reference's
+    fp16-cast provider path only by the fp16 input rounding."""
+    data = load(golden_dir, "sequence_attention.pt")
+    case = data["cases"][2]
+    outs = oracle.sequence_attention(data["q_lin"], data["k_lin"], data["v_lin"], data["wq"], data["wk"],
+                                     data["freqs"], case["heads"], case["world"], data["eps"],
+                                     wire_dtype=torch.float32, attention="sdpa")
+    for r, ref in enumerate(case["ranks"]):
+        err = (outs[r] - ref["out"]).abs()
+        assert float(err.max()) < 2e-2
+        assert float(err.mean() / ref["out"].abs().mean()) < 5e-3
