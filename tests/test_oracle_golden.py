@@ -124,3 +124,10 @@ def test_sdpa_oracle_close_to_reference_path(oracle, golden_dir):
         err = (outs[r] - ref["out"]).abs()
         assert float(err.max()) < 2e-2
         assert float(err.mean() / ref["out"].abs().mean()) < 5e-3
+
+
+def test_product_rope_tables_match_oracle(oracle):
+    from powershard_b200 import rope
+    for grid in ((2, 3, 4), (21, 30, 52)):
+        torch.testing.assert_close(rope.rope_table_3d(grid, 128), oracle.rope_table_3d(grid, 128)[0, :, 0])
+    torch.testing.assert_close(rope.rope_table_flux(5, (4, 6), 128), oracle.rope_table_flux(5, (4, 6), 128)[0, :, 0])
