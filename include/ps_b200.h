@@ -116,6 +116,28 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
                    int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream);
 
+/*
+ * Single-GPU self-attention block that allocates nothing (no counterpart in
+ * the reference).  For callers that may not allocate device memory while
+ * they run - e.g. a plugin host that owns the device-memory budget through
+ * its own pool, or a step that must not hit cudaMalloc's implicit device
+ * synchronisation.  Same math as ps_b200_prepass (world 1, norm_rope 1)
+ * followed by ps_b200_ulysses_attn_fwd (world 1): out [n][heads][head_dim]
+ * in out_dtype.  Its scratch (packed q/k/v and the status word) is a fixed
+ * 96 MiB static device array, so 6 * n * heads * head_dim <= 96 MiB
+ * (n * heads <= 131072 at head_dim 128); larger requests return
+ * PS_B200_ERR_UNSUPPORTED.  Every GPU that uses this entry point keeps the
+ * array until exit.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress), so make it before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race.  If host_status
+ * is not NULL the call synchronizes the stream and stores the kernel's
+ * device status there (0 = ok); with NULL it stays asynchronous.
+ */
+int ps_b200_block_fwd_static(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                             const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,
+                             int64_t freqs_row_stride, void* out, int dtype, int out_dtype, int n, int heads,
+                             int head_dim, float eps, float softmax_scale, int* host_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
