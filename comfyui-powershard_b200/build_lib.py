@@ -15,7 +15,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
-SOURCES = ["csrc/attention.cu", "csrc/prepass.cu", "csrc/capi.cu", "csrc/static_block.cu"]
+SOURCES = ["csrc/attention.cu", "csrc/prepass.cu", "csrc/capi.cu", "csrc/static_block.cu", "csrc/selftest.cu"]
 HEADERS = ["csrc/ptx.cuh", "csrc/internal.h"]
 OUTPUT = HERE / "lib" / "libps_b200.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -41,7 +41,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if up_to_date() and not force:
         return OUTPUT
     OUTPUT.parent.mkdir(parents=True, exist_ok=True)
-    tmp = OUTPUT.with_suffix(".so.tmp")
+    tmp = OUTPUT.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [nvcc(), *ARCH_FLAGS, *FLAGS, "-o", str(tmp), *[str(HERE / s) for s in SOURCES]]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")

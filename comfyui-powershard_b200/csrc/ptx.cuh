@@ -81,24 +81,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of `bar` with the given parity to complete.
-// Returns false (and never blocks longer than kWaitLimitNs) when the wait
-// times out or another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          volatile int* abort_flag, int* status,
-                                          int code) {
+// Returns false (and never blocks longer than limit_ns) when the wait times
+// out or another role of the CTA has already aborted; on a timeout it sets
+// the CTA's abort flag and records `code` in *status (first error wins).
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity,
+                                              volatile int* abort_flag, int* status,
+                                              int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 31u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort_flag = 1;
         if (status) atomicCAS(status, 0, code);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag, int* status,
+                                          int code) {
+  return mbar_wait_for(bar, parity, abort_flag, status, code, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------- TMA

@@ -19,6 +19,8 @@ geometry, dtype) and reused; the returned output is always a fresh tensor.
 """
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
@@ -27,10 +29,18 @@ from .partition import UlyssesGeometry
 
 
 class UlyssesAttention:
-    """Per-rank engine; `group` is the sequence-parallel process group."""
+    """Per-rank engine; `group` is the sequence-parallel process group.
 
-    def __init__(self, group=None):
+    ``kernels`` is the set of device steps (default: the CUDA kernels of
+    ``ops``: ``prepass``, ``ulysses_attention``, ``unpack``, ``DeviceStatus``
+    with the same buffer contracts).  Only tests replace it, to exercise the
+    exchange logic over CPU collectives; CPU tensors given to the default
+    kernels raise.
+    """
+
+    def __init__(self, group=None, kernels=None):
         self.group = group
+        self.kernels = kernels if kernels is not None else ops
         self._buffers = {}
         self._status = {}
 
@@ -46,7 +56,7 @@ class UlyssesAttention:
 
     # ------------------------------------------------------------ buffers
     def _workspace(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
-        stream = torch.cuda.current_stream(device).cuda_stream
+        stream = torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else 0
         key = (device.index, stream, geo.world, geo.width, geo.heads_per_rank, geo.head_dim, dtype)
         ws = self._buffers.get(key)
         if ws is None:
@@ -57,7 +67,7 @@ class UlyssesAttention:
             ws = dict(send=send, recv=recv, out_send=out_send, out_recv=out_recv)
             self._buffers[key] = ws
         if device.index not in self._status:
-            self._status[device.index] = ops.DeviceStatus(device)
+            self._status[device.index] = self.kernels.DeviceStatus(device)
         return ws, self._status[device.index]
 
     def _exchange(self, recv, send, geo):
@@ -85,18 +95,19 @@ class UlyssesAttention:
             raise ValueError("Ulysses local token/head geometry mismatch")
         out_dtype = out_dtype or dtype
         scale = head_dim ** -0.5 if scale is None else float(scale)
-        with torch.cuda.device(device):
+        k = self.kernels
+        with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
             ws, status = self._workspace(geo, dtype, device)
             status.poll()
             out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
-            ops.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope)
+            k.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope)
             self._exchange(ws["recv"], ws["send"], geo)
             if geo.world == 1:
-                ops.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status)
+                k.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status)
             else:
-                ops.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status)
+                k.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status)
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
-                ops.unpack(ws["out_recv"], out, geo)
+                k.unpack(ws["out_recv"], out, geo)
         if state is not None:
             qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
             state["padded_heads"] = geo.padded_heads

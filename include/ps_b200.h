@@ -117,6 +117,14 @@ int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtyp
                    int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream);
 
 /*
+ * Self-test of the bounded waits (no counterpart in the reference): one warp
+ * waits on an mbarrier nothing arrives on for limit_us microseconds (1 ..
+ * 2e6), then writes PS_B200_DEVICE_TIMEOUT_LAST to *status (device int) and
+ * exits; the context stays usable.  Used by the failure-detection tests.
+ */
+int ps_b200_selftest_bounded_wait(int* status, int limit_us, void* stream);
+
+/*
  * Single-GPU self-attention block that allocates nothing (no counterpart in
  * the reference).  For callers that may not allocate device memory while
  * they run - e.g. a plugin host that owns the device-memory budget through

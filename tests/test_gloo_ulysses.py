@@ -1,0 +1,159 @@
+"""The Ulysses exchange logic over real gloo collectives (CPU, no GPU).
+
+``UlyssesAttention`` runs with test-only stand-in kernels (``OracleKernels``)
+that fill the same buffers as the CUDA kernels ([W][3][width][h][D] send,
+[W][width][h][D] output) from the oracle, so these tests check the host side
+of the product path - geometry, buffer reuse, the two all_to_all_single calls,
+padding and the state counters - with real multi-process transport, like the
+reference's tests/test_sequence_distributed.py.  A rank that leaves between
+steps must make the survivor's next exchange raise, not hang.
+"""
+import json
+import os
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _setup_paths():
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import ulysses_oracle
+    return ulysses_oracle
+
+
+class OracleKernels:
+    """Test stand-ins with the buffer contracts of powershard_b200.ops."""
+
+    class DeviceStatus:
+        def __init__(self, device):
+            self.ptr = None
+
+        def poll(self):
+            pass
+
+        def check(self):
+            pass
+
+    @staticmethod
+    def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+        from oracle import ulysses_oracle as oracle
+        n, d = geo.n_local, geo.head_dim
+        if norm_rope:
+            q, k, v = oracle.attention_qkv(x_q[None], x_k[None], x_v[None], w_q, w_k, freqs[None, :, None],
+                                           geo.heads, eps)
+            q, k, v = q[0], k[0], v[0]
+        else:
+            q, k, v = (t.reshape(n, geo.heads, d) for t in (x_q, x_k, x_v))
+        send.copy_(oracle.pack_qkv(q.to(send.dtype), k.to(send.dtype), v.to(send.dtype), geo.total, geo.rank,
+                                   geo.world))
+
+    @staticmethod
+    def ulysses_attention(recv, out_send, geo, scale, status):
+        from oracle import ulysses_oracle as oracle
+        q, k, v = oracle.unpack_qkv(recv, geo.total)
+        o = oracle.sdpa_fp32(q[None], k[None], v[None], scale)[0]
+        packed = oracle.pack_out(o.to(out_send.dtype), geo.total, geo.world)
+        hv = geo.heads_valid
+        out_send[..., :hv, :] = packed[..., :hv, :]
+
+    @staticmethod
+    def unpack(out_recv, out, geo):
+        from oracle import ulysses_oracle as oracle
+        out.copy_(oracle.unpack_out(out_recv, geo.total, geo.heads, geo.rank, geo.world).to(out.dtype))
+
+
+def _inputs(total, heads, oracle):
+    g = torch.Generator().manual_seed(7)
+    x = [torch.randn(1, total, heads * 128, generator=g) for _ in range(3)]
+    wq = torch.rand(heads * 128, generator=g) + 0.5
+    wk = torch.rand(heads * 128, generator=g) + 0.5
+    freqs = oracle.rope_table_3d((total, 1, 1), 128)
+    return x, wq, wk, freqs
+
+
+def exchange_worker(rank, world, store, report, total, heads):
+    oracle = _setup_paths()
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        x, wq, wk, freqs = _inputs(total, heads, oracle)
+        a, b = oracle.shard_bounds(total, rank, world)
+        engine = UlyssesAttention(kernels=OracleKernels)
+        state = {}
+        expected = oracle.sequence_attention(x[0], x[1], x[2], wq, wk, freqs, heads, world,
+                                             wire_dtype=torch.float32)[rank][0]
+        for step in range(2):  # the second step reuses the cached exchange buffers
+            out = engine.forward(x[0][0, a:b], x[1][0, a:b], x[2][0, a:b], wq, wk, freqs[0, a:b, 0],
+                                 total=total, heads=heads, state=state)
+            torch.testing.assert_close(out, expected, atol=1e-5, rtol=1e-5)
+        h = -(-heads // world)
+        width = -(-total // world)
+        assert state["kv_collectives"] == 2 and state["out_collectives"] == 2
+        assert state["padded_heads"] == h * world
+        assert state["kv_gathered_bytes"] == 2 * world * 3 * width * h * 128 * 4
+        assert state["out_exchanged_bytes"] == 2 * world * width * h * 128 * 4
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS", world=world, total=total, heads=heads)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads", [(2, 41, 5), (3, 41, 5), (2, 9, 3), (4, 9, 7)])
+def test_ulysses_engine_over_gloo(world, total, heads, tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    mp.spawn(exchange_worker, args=(world, str(tmp_path / "store"), str(report), total, heads), nprocs=world,
+             join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
+
+
+def leaving_worker(rank, world, store, report):
+    oracle = _setup_paths()
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=8))
+    total, heads = 17, 4
+    x, wq, wk, freqs = _inputs(total, heads, oracle)
+    a, b = oracle.shard_bounds(total, rank, world)
+    engine = UlyssesAttention(kernels=OracleKernels)
+    engine.forward(x[0][0, a:b], x[1][0, a:b], x[2][0, a:b], wq, wk, freqs[0, a:b, 0], total=total, heads=heads)
+    dist.barrier()
+    if rank == 1:
+        os._exit(0)  # leaves between steps: nothing of it is in flight
+    start = time.time()
+    try:
+        engine.forward(x[0][0, a:b], x[1][0, a:b], x[2][0, a:b], wq, wk, freqs[0, a:b, 0], total=total,
+                       heads=heads)
+        result = "completed"
+    except Exception as error:  # the survivor must see an error, not hang
+        result = f"{type(error).__name__}: {str(error)[:200]}"
+    Path(report).write_text(json.dumps(dict(result=result, seconds=time.time() - start)))
+    os._exit(0)  # skip destroy_process_group with a dead peer
+
+
+def test_rank_leaving_makes_survivor_raise(tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    ctx = mp.start_processes(leaving_worker, args=(2, str(tmp_path / "store"), str(report)), nprocs=2,
+                             join=False, start_method="spawn")
+    deadline = time.time() + 120
+    while not ctx.join(timeout=5):
+        if time.time() > deadline:
+            for p in ctx.processes:
+                p.kill()
+            pytest.fail("survivor did not finish within 120 s")
+    data = json.loads(report.read_text())
+    assert data["result"] != "completed", data
+    assert data["seconds"] < 60

@@ -1,0 +1,73 @@
+"""The Ulysses engine over NCCL on several B200s of one node, rank by rank
+against the CPU oracle.  Runs when the box exposes
+at least `world` GPUs; otherwise reported as skipped (NOT_RUN), never passed.
+"""
+import json
+import os
+import socket
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def nccl_worker(rank, world, port, report, total, heads):
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import ulysses_oracle as oracle
+    from powershard_b200.ulysses import UlyssesAttention
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        g = torch.Generator().manual_seed(3)
+        x = [(torch.randn(1, total, heads * 128, generator=g) * 1.4).to(torch.bfloat16) for _ in range(3)]
+        wq = torch.rand(heads * 128, generator=g) + 0.5
+        wk = torch.rand(heads * 128, generator=g) + 0.5
+        freqs = oracle.rope_table_3d((total // 100 + 1, 10, 10), 128)[:, :total]
+        a, b = oracle.shard_bounds(total, rank, world)
+        engine = UlyssesAttention()
+        state = {}
+        outs = []
+        for _ in range(2):
+            outs.append(engine.forward(*(t[0, a:b].to(dev) for t in x), wq.to(dev), wk.to(dev),
+                                       freqs[0, a:b, 0].to(dev), total=total, heads=heads, state=state))
+        engine.check()
+        expected = oracle.sequence_attention(x[0], x[1], x[2], wq, wk, freqs, heads, world)[rank][0].float()
+        errs = []
+        for out in outs:
+            err = (out.float().cpu() - expected).abs()
+            rel = float(err.mean() / expected.abs().mean()) if expected.numel() else 0.0
+            errs.append((float(err.max()) if err.numel() else 0.0, rel))
+        ok = all(e <= 2e-2 and r <= 5e-3 for e, r in errs) and state["kv_collectives"] == 2
+        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads", [(2, 1000, 40), (2, 37, 5), (4, 1023, 40), (8, 4099, 40),
+                                               (3, 300, 24)])
+def test_engine_over_nccl(world, total, heads, tmp_path, cuda_lib):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"NOT_RUN: needs {world} GPUs, box has {torch.cuda.device_count()}")
+    report = tmp_path / "r"
+    mp.spawn(nccl_worker, args=(world, _free_port(), str(report), total, heads), nprocs=world, join=True)
+    for rank in range(world):
+        data = json.loads(Path(f"{report}.{rank}").read_text())
+        assert data["ok"], data
