@@ -10,11 +10,10 @@
 // Warp roles (320 threads):
 //   warps 0-3  softmax + epilogue of query tile 0 (thread = one query row)
 //   warps 4-7  softmax + epilogue of query tile 1
-//   warp  8    TMA producer: Q tiles once, then K_i, V_i into a 4-stage ring
-//   warp  9    TMEM allocator and UMMA issuer (one elected lane)
+//   warp  8    TMA producer: Q tiles once, then K_i / V_i into 2-stage rings
+//   warp  9    TMEM allocator and UMMA issuer (one lane)
 // 10 warps put 3 warps on two of the four SM sub-partitions, which caps a
-// thread at 168 registers; the softmax path is arranged to fit that (the S
-// row is dead before the rare O rescale loads O).
+// thread at 168 registers; the softmax fits that.
 //
 // TMEM (512 columns x 128 lanes, fp32):
 //   [  0,128) S0 = Q0 K^T   (P0, bf16/fp16 pairs, overwrites columns [0,64))
@@ -24,13 +23,21 @@
 // UMMA issue order per key tile i (one thread, in-order tensor pipe):
 //   S0_i = Q0 K_i^T,  O1 += P1_{i-1} V_{i-1},  S1_i = Q1 K_i^T,  O0 += P0_i V_i
 // so while one softmax warpgroup exponentiates, the tensor pipe works on the
-// other tile.  A tcgen05.commit tracks every earlier UMMA of the issuing
-// thread, hence "S_t full" also means the previous O_t update is complete and
-// the softmax warps may rescale O_t in place.
+// other tile, and S_t,i+1 is always issued after the PV that reads P_t,i.
+// A tcgen05.commit tracks every earlier UMMA of the issuing thread, so only
+// two commits per tile are needed: "S_t full" also means O_t's previous update
+// is complete (the softmax warps may rescale O_t in place), and S1_i complete
+// means K_i and V_{i-1} are free (relayed to the producer by a softmax-1
+// thread).  An issuing thread spends ~50 cycles per tcgen05.mma (measured),
+// so the issuer does nothing but wait and issue.
 //
 // Online softmax in the log2 domain with a lazily updated row maximum: the
 // running max m is only raised (and O, l rescaled) when a tile's max exceeds
-// it by more than 8, so P <= 2^8 and rescales are rare after the first tiles.
+// it by more than 8, so P <= 2^8.  P_t is released to the PV UMMAs in two
+// 64-key parts, so the tensor pipe starts on the first half while the softmax
+// writes the second.  The exponentials use ex2.approx on the MUFU; measured on
+// B200, moving part of them to an FMA-pipe polynomial or fusing the row max
+// into the exponential pass made the softmax slower.
 #include "ptx.cuh"
 #include "internal.h"
 
@@ -43,23 +50,35 @@ namespace attn {
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kHeadDim = 128;
-constexpr int kStages = 4;
-constexpr int kTileBytes = kBlockN * kHeadDim * 2;  // 32 KiB: one Q, K or V tile
-constexpr int kHalfTile = kTileBytes / 2;           // one 64-column SW128 half
-constexpr int kThreads = 320;
+constexpr int kKStages = 2;                          // K ring
+constexpr int kVStages = 2;                          // V ring
+constexpr int kTileBytes = kBlockN * kHeadDim * 2;   // 32 KiB: one Q, K or V tile
+constexpr int kHalfTile = kTileBytes / 2;            // one 64-column SW128 half
+constexpr int kThreads = 320;                        // 10 warps
 constexpr int kSmemQ = 2 * kTileBytes;
-constexpr int kSmemKV = kStages * kTileBytes;
-constexpr int kSmemBarOff = kSmemQ + kSmemKV;
+constexpr int kSmemK = kKStages * kTileBytes;
+constexpr int kSmemV = kVStages * kTileBytes;
+constexpr int kSmemBarOff = kSmemQ + kSmemK + kSmemV;
+// P_t is released to the PV UMMAs in kPParts parts of 128/kPParts keys, so
+// the tensor pipe starts on the first keys while the softmax writes the rest.
+#ifndef PSB_P_PARTS
+#define PSB_P_PARTS 2
+#endif
+constexpr int kPParts = PSB_P_PARTS;
+static_assert(kPParts == 1 || kPParts == 2 || kPParts == 4, "P parts: 1, 2 or 4");
+constexpr int kChunksPerPart = 4 / kPParts;  // 32-key chunks per part
 
 enum Bar : int {
   kBarQ = 0,
-  kBarFull = 1,
-  kBarEmpty = kBarFull + kStages,
-  kBarS = kBarEmpty + kStages,
-  kBarP = kBarS + 2,
-  kBarO = kBarP + 2,
-  kBarDrain = kBarO + 1,
-  kNumBars
+  kBarKFull = 1,
+  kBarVFull = kBarKFull + kKStages,
+  kBarS = kBarVFull + kVStages,  // [2] S_t,i computed (issuer commit)
+  kBarFree = kBarS + 2,          // [2] FREE[i%2]: S1_i observed complete -> K_i, V_{i-1} free
+  kBarP = kBarFree + 2,          // [2] P_t written (128 softmax threads)
+  kBarPH = kBarP + 2,            // [2][kPParts-1] leading parts of P_t written
+  kBarO = kBarPH + 2 * (kPParts - 1),  // O_0 and O_1 final
+  kBarDrain = kBarO + 1,         // every UMMA of the issuer complete
+  kNumBars = kBarDrain + 1
 };
 constexpr int kSmemBytes = kSmemBarOff + 256 + 1024;  // barriers + TMEM slot + 1 KiB align slack
 static_assert(kNumBars * 8 + 8 <= 256, "barrier block overflow");
@@ -88,6 +107,22 @@ __device__ __forceinline__ void tile_coord(int t, int full_segs, int tiles_per_s
   }
 }
 
+// Walks the key tiles (segment, first row, valid rows) without divisions.
+struct KeyCursor {
+  int seg = 0, row0 = 0;
+  __device__ __forceinline__ void next(const AttnArgs& a, int& s, int& r, int& valid) {
+    const int seg_len = seg < a.kv_full_segs ? a.seg_rows_k : a.len_k - a.kv_full_segs * a.seg_rows_k;
+    s = seg;
+    r = row0;
+    valid = min(kBlockN, seg_len - row0);
+    row0 += kBlockN;
+    if (row0 >= seg_len) {
+      ++seg;
+      row0 = 0;
+    }
+  }
+};
+
 // Bounded wait whose outcome is uniform across the warp (a lane that timed
 // out drags the whole warp out, so .sync.aligned tcgen05 ops stay converged).
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -113,6 +148,18 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return kFp16 ? pack_f16x2(lo, hi) : pack_bf16x2(lo, hi);
 }
 
+__device__ __forceinline__ float row_max128(const float (&s)[128]) {
+  float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 128; j += 8) {
+    mx0 = fmax3(mx0, s[j], s[j + 1]);
+    mx1 = fmax3(mx1, s[j + 2], s[j + 3]);
+    mx2 = fmax3(mx2, s[j + 4], s[j + 5]);
+    mx3 = fmax3(mx3, s[j + 6], s[j + 7]);
+  }
+  return fmaxf(fmax3(mx0, mx1, mx2), mx3);
+}
+
 template <bool kFp16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -121,7 +168,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + kSmemQ;
+  uint8_t* sK = smem + kSmemQ;
+  uint8_t* sV = sK + kSmemK;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -140,13 +188,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     mbar_init(bar(kBarQ), 1);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarFull + s), 1);
-      mbar_init(bar(kBarEmpty + s), 1);
-    }
+    for (int s = 0; s < kKStages; ++s) mbar_init(bar(kBarKFull + s), 1);
+    for (int s = 0; s < kVStages; ++s) mbar_init(bar(kBarVFull + s), 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(kBarS + t), 1);
+      mbar_init(bar(kBarFree + t), 1);
       mbar_init(bar(kBarP + t), 128);
+      for (int q = 0; q + 1 < kPParts; ++q) mbar_init(bar(kBarPH + t * (kPParts - 1) + q), 128);
     }
     mbar_init(bar(kBarO), 1);
     mbar_init(bar(kBarDrain), 1);
@@ -181,100 +229,118 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_5d(smem_u32(sQ + kTileBytes + c * kHalfTile), &tm_q, bar(kBarQ), c * 64, head, r01,
                     sg1, batch);
       }
-      uint32_t load = 0;
+      // Stage reuse.  The issuer commits S_1,i after S0_i, PV1_{i-1} and S1_i,
+      // so once S1_i is complete K_i and V_{i-1} are no longer read; a
+      // softmax-1 thread then arrives on FREE[i%2].  K_j reuses K_{j-2}'s
+      // stage (signal j-2); V_j reuses V_{j-2}'s stage (signal j-1).  FREE[s]
+      // cannot complete another phase before the producer has loaded the K
+      // tile gated on it, so parity waits never alias.
+      KeyCursor cur;
+      int issued = 0;
       bool ok = true;
       for (int i = 0; i < T && ok; ++i) {
         int seg, row0, valid;
-        tile_coord(i, args.kv_full_segs, args.kv_tiles_per_seg, args.seg_rows_k, args.len_k, seg, row0,
-                   valid);
-        for (int kv = 0; kv < 2; ++kv) {
-          const int stage = load % kStages;
-          const uint32_t phase = (load / kStages) & 1u;
-          ok = mbar_wait(bar(kBarEmpty + stage), phase ^ 1u, abort_flag, status, kErrEmpty);
+        cur.next(args, seg, row0, valid);
+        const int st = i % kKStages;
+        if (i >= kKStages) {
+          ok = mbar_wait(bar(kBarFree + (i & 1)), ((i - 2) >> 1) & 1u, abort_flag, status, kErrEmpty);
           if (!ok) break;
-          mbar_arrive_expect_tx(bar(kBarFull + stage), kTileBytes);
-          const CUtensorMap* map = kv ? &tm_v : &tm_k;
-          uint8_t* dst = sKV + stage * kTileBytes;
-          tma_load_5d(smem_u32(dst), map, bar(kBarFull + stage), 0, kv_head, row0, seg, batch);
-          tma_load_5d(smem_u32(dst + kHalfTile), map, bar(kBarFull + stage), 64, kv_head, row0, seg,
-                      batch);
-          ++load;
         }
+        mbar_arrive_expect_tx(bar(kBarKFull + st), kTileBytes);
+        tma_load_5d(smem_u32(sK + st * kTileBytes), &tm_k, bar(kBarKFull + st), 0, kv_head, row0, seg, batch);
+        tma_load_5d(smem_u32(sK + st * kTileBytes + kHalfTile), &tm_k, bar(kBarKFull + st), 64, kv_head, row0,
+                    seg, batch);
+        issued = 2 * i + 1;
+        if (i >= kVStages) {
+          ok = mbar_wait(bar(kBarFree + ((i - 1) & 1)), ((i - 1) >> 1) & 1u, abort_flag, status, kErrEmpty);
+          if (!ok) break;
+        }
+        mbar_arrive_expect_tx(bar(kBarVFull + st), kTileBytes);
+        tma_load_5d(smem_u32(sV + st * kTileBytes), &tm_v, bar(kBarVFull + st), 0, kv_head, row0, seg, batch);
+        tma_load_5d(smem_u32(sV + st * kTileBytes + kHalfTile), &tm_v, bar(kBarVFull + st), 64, kv_head, row0,
+                    seg, batch);
+        issued = 2 * i + 2;
       }
       // Every copy issued must land before the CTA may exit.
       drain_wait(bar(kBarQ), 0, status);
-      const uint32_t first = load > kStages ? load - kStages : 0;
-      for (uint32_t j = first; j < load; ++j)
-        drain_wait(bar(kBarFull + (j % kStages)), (j / kStages) & 1u, status);
+      const int kv_issued = (issued + 1) / 2;  // key tiles with at least the K copy issued
+      for (int i = max(0, kv_issued - kKStages); i < kv_issued; ++i) {
+        const int st = i % kKStages;
+        const uint32_t ph = (i / kKStages) & 1u;
+        drain_wait(bar(kBarKFull + st), ph, status);
+        if (2 * i + 2 <= issued) drain_wait(bar(kBarVFull + st), ph, status);
+      }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------------ UMMA issuer
+    // ------------------------------------------------------------ UMMA issuer (one lane)
     if (lane == 0) {
       const uint32_t id_qk = idesc_f16(kBlockM, kBlockN, !kFp16, false, false);
       const uint32_t id_pv = idesc_f16(kBlockM, kHeadDim, !kFp16, false, true);
-      const uint32_t sq0 = smem_u32(sQ), sq1 = smem_u32(sQ + kTileBytes);
-      const uint32_t skv = smem_u32(sKV);
-      auto mma_s = [&](int t, int stage) {
-        const uint32_t qa = t ? sq1 : sq0;
-        const uint32_t kb = skv + stage * kTileBytes;
+      // Descriptor bases; per-UMMA offsets are added to the start-address field
+      // (all shared addresses stay below 256 KiB, so the 14-bit field never carries).
+      const uint64_t dq0 = sdesc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dq1 = sdesc_sw128(smem_u32(sQ + kTileBytes), 16, 1024);
+      const uint64_t dk = sdesc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t dv = sdesc_sw128(smem_u32(sV), kHalfTile, 1024);
+      auto mma_s = [&](int t, int st) {
+        const uint64_t dq = t ? dq1 : dq0;
+        const uint64_t dks = dk + static_cast<uint64_t>(st * (kTileBytes >> 4));
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
-          const uint32_t off = (s >> 2) * kHalfTile + (s & 3) * 32;
-          umma_ss(tmem + 128 * t, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), id_qk,
-                  s > 0);
+          const uint32_t off = ((s >> 2) * kHalfTile + (s & 3) * 32) >> 4;
+          umma_ss(tmem + 128 * t, dq + off, dks + off, id_qk, s > 0);
         }
       };
-      auto mma_pv = [&](int t, int stage, bool accumulate) {
-        const uint32_t vb = skv + stage * kTileBytes;
+      // O_t (+)= P_t V for the keys of part q (8/kPParts UMMAs of K=16).
+      auto mma_pv = [&](int t, int st, int q, bool accumulate) {
+        const uint64_t dvs = dv + static_cast<uint64_t>(st * (kTileBytes >> 4));
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          umma_ts(tmem + 256 + 128 * t, tmem + 128 * t + s * 8, sdesc_sw128(vb + s * 2048, kHalfTile, 1024),
-                  id_pv, (accumulate || s > 0) ? 1u : 0u);
+        for (int k = 0; k < 8 / kPParts; ++k) {
+          const int s = (8 / kPParts) * q + k;
+          umma_ts(tmem + 256 + 128 * t, tmem + 128 * t + s * 8, dvs + ((s * 2048) >> 4), id_pv,
+                  (accumulate || s > 0) ? 1u : 0u);
         }
       };
-      auto stage_of = [](uint32_t load) { return static_cast<int>(load % kStages); };
-      auto phase_of = [](uint32_t load) { return (load / kStages) & 1u; };
-
+      // P_t arrives in parts; each part's UMMAs are issued as soon as it is written.
+      auto pv_both = [&](int t, int st, uint32_t parity, bool accumulate) -> bool {
+#pragma unroll
+        for (int q = 0; q < kPParts; ++q) {
+          const int b = q + 1 < kPParts ? kBarPH + t * (kPParts - 1) + q : kBarP + t;
+          if (!mbar_wait(bar(b), parity, abort_flag, status, kErrP)) return false;
+          tc_fence_after();
+          mma_pv(t, st, q, accumulate);
+        }
+        return true;
+      };
+      // Issue order per key tile i: S0_i, PV1_{i-1}, S1_i, PV0_i.
       bool ok = mbar_wait(bar(kBarQ), 0, abort_flag, status, kErrQ);
-      int prev_v = 0;
       for (int i = 0; i < T && ok; ++i) {
-        const uint32_t lk = 2u * i, lv = 2u * i + 1u;
-        ok = mbar_wait(bar(kBarFull + stage_of(lk)), phase_of(lk), abort_flag, status, kErrFull);
+        const int st = i % kKStages;
+        const uint32_t ph = (i / kKStages) & 1u;
+        ok = mbar_wait(bar(kBarKFull + st), ph, abort_flag, status, kErrFull);
         if (!ok) break;
         tc_fence_after();
-        mma_s(0, stage_of(lk));
+        mma_s(0, st);
         umma_commit(bar(kBarS + 0));
         if (i > 0) {
-          ok = mbar_wait(bar(kBarP + 1), (i - 1) & 1u, abort_flag, status, kErrP);
+          ok = pv_both(1, (i - 1) % kVStages, (i - 1) & 1u, i > 1);
           if (!ok) break;
-          tc_fence_after();
-          mma_pv(1, prev_v, i > 1);
-          umma_commit(bar(kBarEmpty + prev_v));
         }
-        mma_s(1, stage_of(lk));
+        mma_s(1, st);
         umma_commit(bar(kBarS + 1));
-        umma_commit(bar(kBarEmpty + stage_of(lk)));
-        ok = mbar_wait(bar(kBarFull + stage_of(lv)), phase_of(lv), abort_flag, status, kErrFull);
-        if (ok) ok = mbar_wait(bar(kBarP + 0), i & 1u, abort_flag, status, kErrP);
+        ok = mbar_wait(bar(kBarVFull + st), ph, abort_flag, status, kErrFull);
+        if (ok) ok = pv_both(0, st, i & 1u, i > 0);
         if (!ok) break;
-        tc_fence_after();
-        mma_pv(0, stage_of(lv), i > 0);
-        prev_v = stage_of(lv);
       }
       if (ok) {
-        ok = mbar_wait(bar(kBarP + 1), (T - 1) & 1u, abort_flag, status, kErrP);
-        if (ok) {
-          tc_fence_after();
-          mma_pv(1, prev_v, T > 1);
-          umma_commit(bar(kBarEmpty + prev_v));
-          umma_commit(bar(kBarO));
-        }
+        ok = pv_both(1, (T - 1) % kVStages, (T - 1) & 1u, T > 1);
+        if (ok) umma_commit(bar(kBarO));
       }
       // All issued UMMAs complete before TMEM is released.
       umma_commit(bar(kBarDrain));
       drain_wait(bar(kBarDrain), 0, status);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ softmax
     const int t = warp >> 2;
     const int quarter = warp & 3;
@@ -285,12 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = args.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    KeyCursor cur;
     for (int i = 0; i < T; ++i) {
-      int seg, row0, valid;
-      tile_coord(i, args.kv_full_segs, args.kv_tiles_per_seg, args.seg_rows_k, args.len_k, seg, row0,
-                 valid);
+      int seg_unused, row_unused, valid;
+      cur.next(args, seg_unused, row_unused, valid);
       ok = warp_wait(bar(kBarS + t), i & 1u, abort_flag, status, kErrS);
       if (!ok) break;
+      if (t == 1 && threadIdx.x == 128) mbar_arrive(bar(kBarFree + (i & 1)));
       tc_fence_after();
       uint32_t sr[128];
       tmem_ld32_at<0>(s_addr + 0, sr);
@@ -301,23 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       float s[128];
 #pragma unroll
       for (int j = 0; j < 128; ++j) s[j] = __uint_as_float(sr[j]);
-      if (valid < kBlockN) {
+      const bool masked = valid < kBlockN;
+      if (masked) {
 #pragma unroll
         for (int j = 0; j < 128; ++j)
           if (j >= valid) s[j] = -INFINITY;
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int j = 4; j < 128; j += 4) {
-        mx0 = fmaxf(mx0, s[j]);
-        mx1 = fmaxf(mx1, s[j + 1]);
-        mx2 = fmaxf(mx2, s[j + 2]);
-        mx3 = fmaxf(mx3, s[j + 3]);
-      }
-      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale_log2;
-      // Raise the running max (warp-uniformly) only when it grew by > 8.
-      float alpha = 1.f;
+      float alpha = 1.f, sum;
       bool rescale = false;
+      // Row max first (lazy running max: raised warp-uniformly only when it
+      // grew by > 8), then the exponentials.
+      const float m_tile = row_max128(s) * scale_log2;
       if (i == 0) {
         m = m_tile;
       } else if (__any_sync(0xffffffffu, m_tile - m > 8.f)) {
@@ -326,32 +387,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
         rescale = true;
       }
-      float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float p0 = ex2_approx(fmaf(s[32 * c + 2 * j], scale_log2, -m));
-          const float p1 = ex2_approx(fmaf(s[32 * c + 2 * j + 1], scale_log2, -m));
-          sum0 += p0;
-          sum1 += p1;
-          pk[j] = pack2<kFp16>(p0, p1);
-        }
-        tmem_st16(s_addr + 16 * c, pk);
-      }
-      l = fmaf(l, alpha, sum0 + sum1);
-      if (rescale) {  // O_t is idle here: its last update completed before S_t was signalled
+      {
+        float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + 32 * c, o);
-          tmem_wait_ld();
+          uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-          tmem_st32(o_addr + 32 * c, o);
+          for (int j = 0; j < 16; ++j) {
+            const float p0 = ex2_approx(fmaf(s[32 * c + 2 * j], scale_log2, -m));
+            const float p1 = ex2_approx(fmaf(s[32 * c + 2 * j + 1], scale_log2, -m));
+            sum0 += p0;
+            sum1 += p1;
+            pk[j] = pack2<kFp16>(p0, p1);
+          }
+          tmem_st16(s_addr + 16 * c, pk);
+          if (c == (kPParts > 1 ? kChunksPerPart - 1 : 3)) {
+            // The rare O rescale goes here, before the first PV part of this
+            // tile is released (O_t's last update completed before S_t was
+            // signalled); the row's first chunks are dead by now.
+            if (rescale) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint32_t o[32];
+                tmem_ld32(o_addr + 32 * q, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+                tmem_st32(o_addr + 32 * q, o);
+              }
+            }
+          }
+          if ((c + 1) % kChunksPerPart == 0 && c < 3) {  // part (c+1)/kChunksPerPart - 1 written
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(kBarPH + t * (kPParts - 1) + (c + 1) / kChunksPerPart - 1));
+          }
         }
+        sum = sum0 + sum1;
       }
+      l = fmaf(l, alpha, sum);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(kBarP + t));
