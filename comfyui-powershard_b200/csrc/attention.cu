@@ -107,10 +107,21 @@ __device__ __forceinline__ void tile_coord(int t, int full_segs, int tiles_per_s
   }
 }
 
-// Walks the key tiles (segment, first row, valid rows) without divisions.
+// Walks the key tiles - the prefix range first, then (segment, first row)
+// of the segmented range - returning the valid rows of each, without divisions.
 struct KeyCursor {
-  int seg = 0, row0 = 0;
-  __device__ __forceinline__ void next(const AttnArgs& a, int& s, int& r, int& valid) {
+  int i = 0, seg = 0, row0 = 0;
+  __device__ __forceinline__ void next(const AttnArgs& a, bool& prefix, int& s, int& r, int& valid) {
+    if (i < a.pre_tiles) {
+      prefix = true;
+      s = 0;
+      r = i * kBlockN;
+      valid = min(kBlockN, a.pre_len - r);
+      ++i;
+      return;
+    }
+    ++i;
+    prefix = false;
     const int seg_len = seg < a.kv_full_segs ? a.seg_rows_k : a.len_k - a.kv_full_segs * a.seg_rows_k;
     s = seg;
     r = row0;
@@ -122,6 +133,19 @@ struct KeyCursor {
     }
   }
 };
+
+// Query tile t: prefix tiles first, then the segmented range.
+__device__ __forceinline__ void q_tile(const AttnArgs& a, int t, bool& prefix, int& seg, int& row0, int& valid) {
+  if (t < a.pre_tiles) {
+    prefix = true;
+    seg = 0;
+    row0 = t * kBlockM;
+    valid = min(kBlockM, a.pre_len - row0);
+  } else {
+    prefix = false;
+    tile_coord(t - a.pre_tiles, a.q_full_segs, a.q_tiles_per_seg, a.seg_rows_q, a.len_q, seg, row0, valid);
+  }
+}
 
 // Bounded wait whose outcome is uniform across the warp (a lane that timed
 // out drags the whole warp out, so .sync.aligned tcgen05 ops stay converged).
@@ -163,7 +187,9 @@ __device__ __forceinline__ float row_max128(const float (&s)[128]) {
 template <bool kFp16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qp,
+                    const __grid_constant__ CUtensorMap tm_kp, const __grid_constant__ CUtensorMap tm_vp,
+                    const AttnArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,18 +241,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
+      bool p0, p1;
       int sg0, r00, v0, sg1, r01, v1;
-      tile_coord(tq0, args.q_full_segs, args.q_tiles_per_seg, args.seg_rows_q, args.len_q, sg0, r00, v0);
+      q_tile(args, tq0, p0, sg0, r00, v0);
       if (tq1 < args.num_q_tiles) {
-        tile_coord(tq1, args.q_full_segs, args.q_tiles_per_seg, args.seg_rows_q, args.len_q, sg1, r01, v1);
+        q_tile(args, tq1, p1, sg1, r01, v1);
       } else {  // no second tile: recompute tile 0, never stored
+        p1 = p0;
         sg1 = sg0;
         r01 = r00;
       }
       mbar_arrive_expect_tx(bar(kBarQ), 2 * kTileBytes);
       for (int c = 0; c < 2; ++c) {
-        tma_load_5d(smem_u32(sQ + c * kHalfTile), &tm_q, bar(kBarQ), c * 64, head, r00, sg0, batch);
-        tma_load_5d(smem_u32(sQ + kTileBytes + c * kHalfTile), &tm_q, bar(kBarQ), c * 64, head, r01,
+        tma_load_5d(smem_u32(sQ + c * kHalfTile), p0 ? &tm_qp : &tm_q, bar(kBarQ), c * 64, head, r00, sg0, batch);
+        tma_load_5d(smem_u32(sQ + kTileBytes + c * kHalfTile), p1 ? &tm_qp : &tm_q, bar(kBarQ), c * 64, head, r01,
                     sg1, batch);
       }
       // Stage reuse.  The issuer commits S_1,i after S0_i, PV1_{i-1} and S1_i,
@@ -239,26 +267,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < T && ok; ++i) {
+        bool pre;
         int seg, row0, valid;
-        cur.next(args, seg, row0, valid);
+        cur.next(args, pre, seg, row0, valid);
+        const CUtensorMap* mk = pre ? &tm_kp : &tm_k;
+        const CUtensorMap* mv = pre ? &tm_vp : &tm_v;
         const int st = i % kKStages;
         if (i >= kKStages) {
           ok = mbar_wait(bar(kBarFree + (i & 1)), ((i - 2) >> 1) & 1u, abort_flag, status, kErrEmpty);
           if (!ok) break;
         }
         mbar_arrive_expect_tx(bar(kBarKFull + st), kTileBytes);
-        tma_load_5d(smem_u32(sK + st * kTileBytes), &tm_k, bar(kBarKFull + st), 0, kv_head, row0, seg, batch);
-        tma_load_5d(smem_u32(sK + st * kTileBytes + kHalfTile), &tm_k, bar(kBarKFull + st), 64, kv_head, row0,
-                    seg, batch);
+        tma_load_5d(smem_u32(sK + st * kTileBytes), mk, bar(kBarKFull + st), 0, kv_head, row0, seg, batch);
+        tma_load_5d(smem_u32(sK + st * kTileBytes + kHalfTile), mk, bar(kBarKFull + st), 64, kv_head, row0, seg,
+                    batch);
         issued = 2 * i + 1;
         if (i >= kVStages) {
           ok = mbar_wait(bar(kBarFree + ((i - 1) & 1)), ((i - 1) >> 1) & 1u, abort_flag, status, kErrEmpty);
           if (!ok) break;
         }
         mbar_arrive_expect_tx(bar(kBarVFull + st), kTileBytes);
-        tma_load_5d(smem_u32(sV + st * kTileBytes), &tm_v, bar(kBarVFull + st), 0, kv_head, row0, seg, batch);
-        tma_load_5d(smem_u32(sV + st * kTileBytes + kHalfTile), &tm_v, bar(kBarVFull + st), 64, kv_head, row0,
-                    seg, batch);
+        tma_load_5d(smem_u32(sV + st * kTileBytes), mv, bar(kBarVFull + st), 0, kv_head, row0, seg, batch);
+        tma_load_5d(smem_u32(sV + st * kTileBytes + kHalfTile), mv, bar(kBarVFull + st), 64, kv_head, row0, seg,
+                    batch);
         issued = 2 * i + 2;
       }
       // Every copy issued must land before the CTA may exit.
@@ -353,8 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     KeyCursor cur;
     for (int i = 0; i < T; ++i) {
+      bool pre_unused;
       int seg_unused, row_unused, valid;
-      cur.next(args, seg_unused, row_unused, valid);
+      cur.next(args, pre_unused, seg_unused, row_unused, valid);
       ok = warp_wait(bar(kBarS + t), i & 1u, abort_flag, status, kErrS);
       if (!ok) break;
       if (t == 1 && threadIdx.x == 128) mbar_arrive(bar(kBarFree + (i & 1)));
@@ -434,13 +466,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     if (ok) {
       const int tq = t ? tq1 : tq0;
+      bool pre = false;
       int seg = 0, row0 = 0, valid = 0;
-      if (tq < args.num_q_tiles)
-        tile_coord(tq, args.q_full_segs, args.q_tiles_per_seg, args.seg_rows_q, args.len_q, seg, row0, valid);
+      if (tq < args.num_q_tiles) q_tile(args, tq, pre, seg, row0, valid);
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const bool store = row < valid;
-      const int64_t oidx = batch * args.o_stride[0] + seg * args.o_stride[1] +
-                           static_cast<int64_t>(row0 + row) * args.o_stride[2] + head * args.o_stride[3];
+      void* const obase = pre ? args.pre_out : args.out;
+      const int64_t* ost = pre ? args.pre_o_stride : args.o_stride;
+      const int64_t oidx = batch * ost[0] + seg * ost[1] + static_cast<int64_t>(row0 + row) * ost[2] +
+                           head * ost[3];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
@@ -448,13 +482,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if (store) {
           if (args.out_fp32) {
-            float4* orow = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + oidx + 32 * c);
+            float4* orow = reinterpret_cast<float4*>(reinterpret_cast<float*>(obase) + oidx + 32 * c);
 #pragma unroll
             for (int u = 0; u < 8; ++u)
               orow[u] = make_float4(__uint_as_float(o[4 * u + 0]) * inv_l, __uint_as_float(o[4 * u + 1]) * inv_l,
                                     __uint_as_float(o[4 * u + 2]) * inv_l, __uint_as_float(o[4 * u + 3]) * inv_l);
           } else {
-            uint16_t* orow = reinterpret_cast<uint16_t*>(args.out) + oidx + 32 * c;
+            uint16_t* orow = reinterpret_cast<uint16_t*>(obase) + oidx + 32 * c;
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               uint4 v;
@@ -490,16 +524,17 @@ int prepare_kernel() {
 }  // namespace
 
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const CUtensorMap& tqp, const CUtensorMap& tkp, const CUtensorMap& tvp,
                      const AttnArgs& args, int heads_q, int batch, bool fp16, cudaStream_t stream) {
   using namespace attn;
   const dim3 grid((args.num_q_tiles + 1) / 2, heads_q, batch);
   const dim3 block(kThreads);
   if (fp16) {
     if (int rc = prepare_kernel<true>()) return rc;
-    attn_fwd_kernel<true><<<grid, block, kSmemBytes, stream>>>(tq, tk, tv, args);
+    attn_fwd_kernel<true><<<grid, block, kSmemBytes, stream>>>(tq, tk, tv, tqp, tkp, tvp, args);
   } else {
     if (int rc = prepare_kernel<false>()) return rc;
-    attn_fwd_kernel<false><<<grid, block, kSmemBytes, stream>>>(tq, tk, tv, args);
+    attn_fwd_kernel<false><<<grid, block, kSmemBytes, stream>>>(tq, tk, tv, tqp, tkp, tvp, args);
   }
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return set_cuda_error("attention launch", err);

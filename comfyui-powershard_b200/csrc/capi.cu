@@ -94,19 +94,30 @@ struct SegTensor {
   int heads;  // extent of the head axis in the map
 };
 
+// Optional prefix range (joint attention): queries/keys [0, len) from its own
+// tensors, ahead of the segmented range.
+struct Prefix {
+  SegTensor q, k, v;
+  void* out = nullptr;
+  int64_t out_st[4] = {0, 0, 0, 0};
+  int len = 0;
+};
+
 int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v, void* out,
                      const int64_t out_st[4], int dtype, int out_dtype, int batch, int grid_heads, int group,
                      int head_dim,
                      int seg_rows_q, int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k,
-                     float softmax_scale, int* status, void* stream) {
+                     float softmax_scale, int* status, void* stream, const Prefix* pre = nullptr) {
+  const int pre_len = pre ? pre->len : 0;
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "attention supports bf16 and fp16 only");
   if (out_dtype != dtype && out_dtype != PS_B200_FP32)
     return set_error(PS_B200_ERR_UNSUPPORTED, "attention output must be fp32 or the input dtype");
   if (head_dim != 128) return set_error(PS_B200_ERR_UNSUPPORTED, "attention supports head_dim 128 only (got %d)", head_dim);
   if (batch < 0 || grid_heads < 0 || len_q < 0 || len_k < 0 || group < 1)
     return set_error(PS_B200_ERR_INVALID, "negative size");
-  if (batch == 0 || grid_heads == 0 || len_q == 0) return PS_B200_OK;
-  if (len_k == 0) return set_error(PS_B200_ERR_INVALID, "empty key set");
+  if (pre_len < 0) return set_error(PS_B200_ERR_INVALID, "negative prefix length");
+  if (batch == 0 || grid_heads == 0 || len_q + pre_len == 0) return PS_B200_OK;
+  if (len_k + pre_len == 0) return set_error(PS_B200_ERR_INVALID, "empty key set");
   if (seg_rows_q <= 0 || segs_q <= 0 || seg_rows_k <= 0 || segs_k <= 0)
     return set_error(PS_B200_ERR_INVALID, "segment geometry must be positive");
   if (int64_t(seg_rows_q) * segs_q < len_q || int64_t(seg_rows_k) * segs_k < len_k)
@@ -116,6 +127,15 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
   if (!q.ptr || !k.ptr || !v.ptr || !out) return set_error(PS_B200_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q.ptr) || !aligned16(k.ptr) || !aligned16(v.ptr) || !aligned16(out))
     return set_error(PS_B200_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if (pre_len) {
+    if (!pre->q.ptr || !pre->k.ptr || !pre->v.ptr || !pre->out)
+      return set_error(PS_B200_ERR_INVALID, "null prefix tensor pointer");
+    if (!aligned16(pre->q.ptr) || !aligned16(pre->k.ptr) || !aligned16(pre->v.ptr) || !aligned16(pre->out))
+      return set_error(PS_B200_ERR_INVALID, "prefix tensor pointers must be 16-byte aligned");
+    for (int i = 0; i < 4; ++i)
+      if (pre->out_st[i] < 0 || pre->out_st[i] % 8 != 0)
+        return set_error(PS_B200_ERR_INVALID, "prefix output strides must be non-negative multiples of 8");
+  }
   for (int i = 0; i < 4; ++i)
     if (out_st[i] < 0 || out_st[i] % 8 != 0)
       return set_error(PS_B200_ERR_INVALID, "output strides must be non-negative multiples of 8 elements");
@@ -127,6 +147,12 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
   if (int rc = make_map(&tq, q.ptr, fp16, head_dim, q.heads, seg_rows_q, segs_q, batch, q.st)) return rc;
   if (int rc = make_map(&tk, k.ptr, fp16, head_dim, k.heads, seg_rows_k, segs_k, batch, k.st)) return rc;
   if (int rc = make_map(&tv, v.ptr, fp16, head_dim, v.heads, seg_rows_k, segs_k, batch, v.st)) return rc;
+  CUtensorMap tqp = tq, tkp = tk, tvp = tv;
+  if (pre_len) {
+    if (int rc = make_map(&tqp, pre->q.ptr, fp16, head_dim, pre->q.heads, pre_len, 1, batch, pre->q.st)) return rc;
+    if (int rc = make_map(&tkp, pre->k.ptr, fp16, head_dim, pre->k.heads, pre_len, 1, batch, pre->k.st)) return rc;
+    if (int rc = make_map(&tvp, pre->v.ptr, fp16, head_dim, pre->v.heads, pre_len, 1, batch, pre->v.st)) return rc;
+  }
   AttnArgs a{};
   a.out = out;
   for (int i = 0; i < 4; ++i) a.o_stride[i] = out_st[i];
@@ -140,7 +166,13 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
   a.scale_log2 = static_cast<float>(double(softmax_scale) * 1.4426950408889634);
   a.out_fp32 = out_dtype == PS_B200_FP32;
   a.status = status;
-  return launch_attention(tq, tk, tv, a, grid_heads, batch, fp16, static_cast<cudaStream_t>(stream));
+  a.pre_len = pre_len;
+  a.pre_tiles = (pre_len + 127) / 128;
+  a.num_q_tiles += a.pre_tiles;
+  a.num_kv_tiles += a.pre_tiles;
+  a.pre_out = pre_len ? pre->out : out;
+  for (int i = 0; i < 4; ++i) a.pre_o_stride[i] = pre_len ? pre->out_st[i] : out_st[i];
+  return launch_attention(tq, tk, tv, tqp, tkp, tvp, a, grid_heads, batch, fp16, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -176,6 +208,9 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
       int64_t(heads_per_rank) * world < heads || head_dim <= 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent prepass geometry");
   if (head_dim % 8 != 0) return set_error(PS_B200_ERR_UNSUPPORTED, "head_dim must be a multiple of 8");
+  if (norm_rope < 0 || norm_rope > 2) return set_error(PS_B200_ERR_INVALID, "norm_rope must be 0, 1 or 2");
+  if (norm_rope == 2 && (head_dim / 8 > 32 || ((head_dim / 8) & (head_dim / 8 - 1)) != 0))
+    return set_error(PS_B200_ERR_UNSUPPORTED, "per-head norm needs head_dim/8 a power of two <= 32");
   if (int64_t(heads) * head_dim > 8192)
     return set_error(PS_B200_ERR_UNSUPPORTED, "heads*head_dim above 8192 is not supported");
   if (seg_rows == 0) return PS_B200_OK;
@@ -250,6 +285,41 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
   SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows, world, total,
                           seg_rows, world, total, softmax_scale, status, stream);
+}
+
+int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
+                                   int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
+                                   int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
+                                   int* status, void* stream) {
+  if (world < 1 || seg_rows < 1 || total < 1 || prefix_len < 0 || heads_per_rank < 1 || heads_valid < 0 ||
+      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent joint Ulysses geometry");
+  if (heads_valid == 0) return PS_B200_OK;
+  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows, P = prefix_len;
+  const int64_t block = n * h * D;
+  const char* base = static_cast<const char*>(recv);
+  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
+  const int64_t out_st[4] = {int64_t(world) * block, block, h * D, D};
+  SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  Prefix pre;
+  pre.len = prefix_len;
+  if (prefix_len) {
+    const char* pb = static_cast<const char*>(prefix_qkv);
+    const int64_t pblock = P * h * D;
+    const int64_t pst[4] = {3 * pblock, 3 * pblock, h * D, D};
+    pre.q = SegTensor{pb, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.k = SegTensor{pb + pblock * 2, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.v = SegTensor{pb + pblock * 4, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.out = prefix_out;
+    pre.out_st[0] = pblock;
+    pre.out_st[1] = pblock;
+    pre.out_st[2] = h * D;
+    pre.out_st[3] = D;
+  }
+  return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
+                          world, total, seg_rows, world, total, softmax_scale, status, stream, &pre);
 }
 
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,

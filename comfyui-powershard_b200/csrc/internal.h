@@ -25,9 +25,17 @@ struct AttnArgs {
   float scale_log2;      // softmax_scale * log2(e)
   int out_fp32;          // 1: output fp32, 0: output in the input 16-bit type
   int* status;           // device status word (0 = ok), may be null
+  // Optional prefix range (Flux text tokens): query and key rows [0, pre_len)
+  // come from the prefix maps, ahead of the segmented rows; num_q_tiles and
+  // num_kv_tiles count both ranges.  pre_len == 0: no prefix.
+  int pre_len;
+  int pre_tiles;         // ceil(pre_len / 128)
+  void* pre_out;         // prefix output row 0, head 0
+  int64_t pre_o_stride[4];  // batch, (unused), row, head strides in elements
 };
 
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                     const CUtensorMap& tqp, const CUtensorMap& tkp, const CUtensorMap& tvp,
                      const AttnArgs& args, int heads_q, int batch, bool fp16, cudaStream_t stream);
 
 struct PrepassArgs {
@@ -40,7 +48,7 @@ struct PrepassArgs {
   void* send;              // [world][3][seg_rows][heads_per_rank][head_dim]
   int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
   float eps;
-  int norm_rope;           // 1: RMSNorm + RoPE on q and k, 0: plain pack
+  int norm_rope;           // 0: plain pack, 1: full-width RMSNorm + RoPE, 2: per-head RMSNorm + RoPE
 };
 
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);

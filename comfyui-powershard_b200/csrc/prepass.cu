@@ -2,8 +2,10 @@
 // Ulysses pack ("pre-pass") and the receive-side head->sequence unpack.
 //
 // Pre-pass, one CTA per token row of the send segment (seg_rows CTAs):
-//   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)      (RMSNorm, full width)
-//         out[2j], out[2j+1] = F[j] @ (y[2j], y[2j+1])           (interleaved RoPE)
+//   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)   (RMSNorm over the
+//         full width (Wan, norm_rope 1) or over each head (Flux QK-norm,
+//         norm_rope 2, weight [head_dim] shared by the heads))
+//         out[2j], out[2j+1] = F[j] @ (y[2j], y[2j+1])     (interleaved RoPE)
 //   v   : copied.
 // Each result goes straight to its slot of the all-to-all send buffer
 // [world][3][seg_rows][heads_per_rank][head_dim]: global head g lands in
@@ -74,7 +76,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 template <bool kFp16>
-__global__ void __launch_bounds__(kThreads) prepass_kernel(const PrepassArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs a) {
   __shared__ float red[kThreads / 32];
   const int i = blockIdx.x;
   const int tid = threadIdx.x;
@@ -103,15 +105,17 @@ __global__ void __launch_bounds__(kThreads) prepass_kernel(const PrepassArgs a) 
   }
 
   const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
+  const bool per_head = a.norm_rope == 2;  // Flux QK-norm: statistic per head, weight [head_dim]
 #pragma unroll
   for (int kind = 0; kind < 3; ++kind) {
     const uint16_t* x = static_cast<const uint16_t*>(a.x[kind]) + static_cast<int64_t>(i) * a.x_row_stride[kind];
     const bool normed = kind < 2 && a.norm_rope;
     uint4 xv[kMaxVec];
-    float ss = 0.f;
+    float ss[kMaxVec];
 #pragma unroll
     for (int u = 0; u < kMaxVec; ++u) {
       const int v = tid + u * kThreads;
+      ss[u] = 0.f;
       if (v < nvec) {
         xv[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(v) * 8));
         if (normed) {
@@ -120,16 +124,31 @@ __global__ void __launch_bounds__(kThreads) prepass_kernel(const PrepassArgs a) 
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float f = to_f<kFp16>(e[q]);
-            ss = fmaf(f, f, ss);
+            ss[u] = fmaf(f, f, ss[u]);
           }
         }
       }
     }
-    float r = 1.f;
-    if (normed) {
-      const float total = block_sum(ss, red);
+    float r[kMaxVec];
+    if (normed && !per_head) {
+      float tot = 0.f;
+#pragma unroll
+      for (int u = 0; u < kMaxVec; ++u) tot += ss[u];
+      const float total = block_sum(tot, red);
       const float mean = __fdiv_rn(total, static_cast<float>(a.heads * D));
-      r = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+      const float rr = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+#pragma unroll
+      for (int u = 0; u < kMaxVec; ++u) r[u] = rr;
+    } else if (normed) {
+      // The vph (= D/8, a power of two <= 32) consecutive lanes holding one
+      // head reduce their partial sums with xor shuffles.
+#pragma unroll
+      for (int u = 0; u < kMaxVec; ++u) {
+        float t = ss[u];
+        for (int o = vph >> 1; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        const float mean = __fdiv_rn(t, static_cast<float>(D));
+        r[u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+      }
     }
 #pragma unroll
     for (int u = 0; u < kMaxVec; ++u) {
@@ -142,18 +161,20 @@ __global__ void __launch_bounds__(kThreads) prepass_kernel(const PrepassArgs a) 
         uint16_t e[8];
         unpack8(xv[u], e);
         float y[8];
+        const int widx = per_head ? dd : v * 8;  // weight element of this vector's first value
         if (a.w_fp32) {
-          const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + v * 8);
+          const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + widx);
           const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
           const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int q = 0; q < 8; ++q) y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r), w[q])));
+          for (int q = 0; q < 8; ++q)
+            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[u]), w[q])));
         } else {
           uint16_t we[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + v * 8)), we);
+          unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + widx)), we);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r), to_f<kFp16>(we[q]))));
+            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[u]), to_f<kFp16>(we[q]))));
         }
         // RoPE: pair p of this vector is pair (dd/2 + p) of the head.
         const float4* fp = reinterpret_cast<const float4*>(frow) + (dd >> 1);

@@ -57,13 +57,18 @@ def _check16(t: torch.Tensor, what: str):
         raise _lib.UnsupportedAttention(f"{what}: bf16/fp16 required, got {t.dtype}")
 
 
+NORM_NONE, NORM_FULL, NORM_PER_HEAD = 0, 1, 2
+
+
 def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: float = 1e-6,
-            norm_rope: bool = True):
+            norm_rope=True):
     """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
 
-    x_*: [n_local, H*D] (row stride may exceed H*D); w_*: [H*D]; freqs:
-    [n_local, D/2, 2, 2] fp32 (ignored when norm_rope is False).
+    x_*: [n_local, H*D] (row stride may exceed H*D); freqs: [n_local, D/2, 2, 2]
+    fp32.  norm_rope: False/0 pack only, True/1 RMSNorm over the full width
+    (Wan; w_* [H*D]), 2 RMSNorm per head (Flux QK-norm; w_* [D]).
     """
+    mode = int(norm_rope)
     lib = _lib.load()
     for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v"), (send, "send")):
         _check16(t, f"prepass {name}")
@@ -80,10 +85,11 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
     w_dtype = _lib.dtype_code(send.dtype)
     fptr, fstride = 0, 0
     wq = wk = 0
-    if norm_rope:
+    if mode:
+        wlen = width if mode == NORM_FULL else geo.head_dim
         for t, name in ((w_q, "w_q"), (w_k, "w_k")):
-            if t.dim() != 1 or t.shape[0] != width or not t.is_contiguous() or t.device != send.device:
-                raise ValueError(f"prepass {name}: expected contiguous [{width}] on {send.device}")
+            if t.dim() != 1 or t.shape[0] != wlen or not t.is_contiguous() or t.device != send.device:
+                raise ValueError(f"prepass {name}: expected contiguous [{wlen}] on {send.device}")
         if w_q.dtype != w_k.dtype:
             raise ValueError("prepass: norm weights must share a dtype")
         w_dtype = _lib.dtype_code(w_q.dtype)
@@ -99,7 +105,7 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
         _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]),
         wq, wk, w_dtype, fptr, fstride, send.data_ptr(), _lib.dtype_code(send.dtype),
         geo.world, n, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
-        1 if norm_rope else 0, _lib.stream_handle(send.device))
+        mode, _lib.stream_handle(send.device))
     _lib.check(rc, "ps_b200_prepass")
 
 
@@ -119,6 +125,36 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
         geo.world, geo.width, geo.total, geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale),
         status.ptr if status is not None else None, _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_attn_fwd")
+    if status is not None:
+        status.arm()
+
+
+def ulysses_joint_attention(recv, prefix_qkv, out_send, prefix_out, geo: UlyssesGeometry, scale: float,
+                            status: DeviceStatus | None):
+    """Joint attention: this rank's text rows prefix_qkv [3,P,h,D] ahead of the
+    image rows of recv [W,3,width,h,D]; text outputs -> prefix_out [P,h,D],
+    image outputs -> out_send [W,width,h,D]."""
+    lib = _lib.load()
+    _check16(recv, "joint attention recv")
+    _check16(prefix_qkv, "joint attention prefix")
+    if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
+        raise ValueError(f"joint attention: recv must be contiguous {geo.send_shape()}")
+    h, d = geo.heads_per_rank, geo.head_dim
+    if prefix_qkv.dim() != 4 or tuple(prefix_qkv.shape[::2]) != (3, h) or prefix_qkv.shape[3] != d \
+            or not prefix_qkv.is_contiguous() or prefix_qkv.dtype != recv.dtype:
+        raise ValueError(f"joint attention: prefix must be contiguous [3, P, {h}, {d}]")
+    plen = prefix_qkv.shape[1]
+    for t, shape, name in ((out_send, geo.out_shape(), "out"), (prefix_out, (plen, h, d), "prefix out")):
+        if tuple(t.shape) != tuple(shape) or not t.is_contiguous() or t.dtype not in (recv.dtype, torch.float32):
+            raise ValueError(f"joint attention: {name} must be contiguous {tuple(shape)}")
+    if out_send.dtype != prefix_out.dtype:
+        raise ValueError("joint attention: both outputs need the same dtype")
+    rc = lib.ps_b200_ulysses_joint_attn_fwd(
+        recv.data_ptr(), prefix_qkv.data_ptr(), out_send.data_ptr(), prefix_out.data_ptr(),
+        _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype), geo.world, geo.width, geo.total, plen,
+        h, geo.heads_valid, d, float(scale), status.ptr if status is not None else None,
+        _lib.stream_handle(recv.device))
+    _lib.check(rc, "ps_b200_ulysses_joint_attn_fwd")
     if status is not None:
         status.arm()
 

@@ -57,6 +57,12 @@ class UlyssesGeometry:
         h = self.heads_per_rank
         return max(0, min(h, self.heads - self.rank * h))
 
+    @classmethod
+    def replicated(cls, rows: int, heads: int, head_dim: int, world: int) -> "UlyssesGeometry":
+        """Geometry that packs `rows` tokens held by every rank (Flux text) for
+        all W head blocks: rank 0 of a rows*W sequence has exactly those rows."""
+        return cls(total=rows * world, heads=heads, head_dim=head_dim, world=world, rank=0)
+
     def send_shape(self):
         return (self.world, 3, self.width, self.heads_per_rank, self.head_dim)
 

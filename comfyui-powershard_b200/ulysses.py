@@ -118,6 +118,65 @@ class UlyssesAttention:
             state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
         return out
 
+    def forward_joint(self, txt, img, w_q, w_k, txt_freqs, img_freqs, *, total_img: int, heads: int,
+                      eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
+                      norm: int = ops.NORM_PER_HEAD, state: dict | None = None):
+        """Flux joint attention: text rows replicated on every rank, image rows Ulysses-split.
+
+        txt = (q, k, v) [P, H*D] projections of the P text tokens (identical on
+        every rank); img = (q, k, v) [n_img_local, H*D] of this rank's image
+        tokens (shard_bounds of total_img); txt_freqs [P, D/2, 2, 2] and
+        img_freqs [n_img_local, D/2, 2, 2].  Keys and queries of every head
+        are [text; all image tokens].  Only image rows cross the all-to-all;
+        each rank attends text queries for its own heads and the text outputs
+        are all-gathered over heads.  Returns (txt_out [P, H, D],
+        img_out [n_img_local, H, D]) in out_dtype.
+        """
+        device = img[0].device
+        dtype = img[0].dtype
+        head_dim = img[0].shape[-1] // heads
+        geo = self.geometry(total_img, heads, head_dim)
+        if img[0].shape[0] != geo.n_local:
+            raise ValueError("Ulysses local token/head geometry mismatch")
+        plen = txt[0].shape[0]
+        tgeo = UlyssesGeometry.replicated(plen, heads, head_dim, geo.world)
+        out_dtype = out_dtype or dtype
+        scale = head_dim ** -0.5 if scale is None else float(scale)
+        k = self.kernels
+        with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
+            ws, status = self._workspace(geo, dtype, device)
+            status.poll()
+            tkey = ("txt", device.index, plen, geo.world, geo.heads_per_rank, head_dim, dtype)
+            if tkey not in self._buffers:  # text rows: packed q/k/v and this rank's heads' outputs (wire dtype)
+                self._buffers[tkey] = dict(
+                    send=torch.empty(tgeo.send_shape(), dtype=dtype, device=device),
+                    out=torch.empty((plen, geo.heads_per_rank, head_dim), dtype=dtype, device=device))
+            tb = self._buffers[tkey]
+            img_out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
+            txt_out = torch.empty((plen, heads, head_dim), dtype=out_dtype, device=device)
+            k.prepass(*txt, w_q, w_k, txt_freqs, tb["send"], tgeo, eps, norm)
+            k.prepass(*img, w_q, w_k, img_freqs, ws["send"], geo, eps, norm)
+            self._exchange(ws["recv"], ws["send"], geo)
+            prefix = tb["send"][geo.rank]
+            if geo.world == 1:
+                k.ulysses_joint_attention(ws["recv"], prefix, img_out.view(geo.out_shape()), txt_out, geo, scale,
+                                          status)
+            else:
+                k.ulysses_joint_attention(ws["recv"], prefix, ws["out_send"], tb["out"], geo, scale, status)
+                self._exchange(ws["out_recv"], ws["out_send"], geo)
+                k.unpack(ws["out_recv"], img_out, geo)
+                gathered = torch.empty((geo.world,) + tuple(tb["out"].shape), dtype=dtype, device=device)
+                dist.all_gather_into_tensor(gathered, tb["out"], group=self.group)
+                k.unpack(gathered, txt_out, tgeo)
+        if state is not None:
+            qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+            state["padded_heads"] = geo.padded_heads
+            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
+            state["out_collectives"] = state.get("out_collectives", 0) + 2
+            state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
+        return txt_out, img_out
+
     def check(self):
         """Synchronize and raise if any attention launch aborted on the device."""
         for status in self._status.values():

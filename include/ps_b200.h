@@ -68,12 +68,13 @@ const char* ps_b200_last_error(void);
  * send-side packing of ulysses_to_sequence).
  *   x_q, x_k, x_v  [n_local][heads*head_dim] projection outputs (dtype), row
  *                  strides x_row_strides[0..2] in elements (16-byte aligned).
- *   w_qnorm, w_knorm [heads*head_dim] RMSNorm weights, w_dtype = dtype or FP32.
+ *   w_qnorm, w_knorm RMSNorm weights, w_dtype = dtype or FP32: [heads*head_dim]
+ *                  for norm_rope 1, [head_dim] (shared by all heads) for 2.
  *   freqs          [n_local][head_dim/2][2][2] fp32 rotation table (the
  *                  reference's freqs[0, :, 0]), freqs_row_stride in floats.
  *   send           [world][3][seg_rows][heads_per_rank][head_dim] (dtype).
- *   norm_rope      1: RMSNorm + RoPE on q and k (Wan self-attention),
- *                  0: pack only.
+ *   norm_rope      1: RMSNorm over the full width + RoPE on q and k (Wan),
+ *                  2: RMSNorm over each head + RoPE (Flux QK-norm), 0: pack only.
  * Rows n_local..seg_rows-1 and heads heads..world*heads_per_rank-1 of the
  * send buffer are written as zeros.
  */
@@ -107,6 +108,21 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
                              int total, int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
                              int* status, void* stream);
+
+/*
+ * Joint attention (Flux: text tokens replicated on every rank, image tokens
+ * Ulysses-split): keys and queries are the rank's text rows prefix_qkv
+ * [3][prefix_len][heads_per_rank][head_dim] followed by the image rows of the
+ * receive buffer recv (as in ps_b200_ulysses_attn_fwd).  Text query outputs
+ * go to prefix_out [prefix_len][heads_per_rank][head_dim], image query
+ * outputs to out_send.  No counterpart call in the reference, which
+ * all-gathers K/V for this model (powershard/image_parallel.py:96-110); the
+ * result equals attention over [text; image] (ComfyUI Flux joint attention).
+ */
+int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
+                                   int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
+                                   int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
+                                   int* status, void* stream);
 
 /*
  * Inverse unpack: recv [world][seg_rows][heads_per_rank][head_dim] (dtype)

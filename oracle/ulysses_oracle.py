@@ -31,7 +31,7 @@ __all__ = [
     "shard_bounds", "rms_norm", "rope_apply", "rope_axes", "rope_table_3d",
     "rope_table_flux", "attention_qkv", "pack_qkv", "exchange", "unpack_qkv",
     "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention",
-    "time_reference_sample",
+    "rms_norm_heads", "flux_joint_attention", "time_reference_sample",
 ]
 
 
@@ -288,6 +288,46 @@ def sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: in
         outs.append(pack_out(o.to(wire_dtype), total, world))
     back = exchange(outs)
     return [unpack_out(back[r], total, heads, r, world)[None] for r in range(world)]
+
+
+# ------------------------------------------------- Flux joint attention
+def rms_norm_heads(x, weight, heads: int, eps: float = 1e-6):
+    """Per-head RMSNorm (Flux QK-norm): [B,n,H*D] -> [B,n,H,D], weight [D].
+
+    Same fp32-statistic / cast-back semantics as operations.RMSNorm
+    (powershard/operations.py:61-64), applied over each head's D values.
+    Restates ComfyUI's Flux QKNorm (not in the reference tree): unpinned.
+    """
+    b, n, width = x.shape
+    y = x.view(b, n, heads, width // heads).float()
+    y = y * torch.rsqrt(y.square().mean(-1, keepdim=True) + eps)
+    return (y * weight.float()).to(x.dtype)
+
+
+def flux_joint_attention(txt, img, wq, wk, txt_freqs, img_freqs, heads: int, world: int, eps: float = 1e-6,
+                         wire_dtype=torch.bfloat16, scale=None):
+    """Flux joint attention of one double/single block, ranks simulated.
+
+    txt = (q, k, v) [1, P, H*D] text projections (replicated on every rank),
+    img = (q, k, v) [1, L, H*D] image projections (rank r owns
+    shard_bounds(L, r, W)); freqs tables [1, n, 1, D/2, 2, 2].  Keys and
+    queries are [text; image] (powershard/image_parallel.py:96-110 computes
+    the same attention with a K/V all-gather).  Returns per rank
+    (text out [P, H, D], image out [n_r, H, D]) in the wire dtype.
+    """
+    def qk(x, w, f):
+        return rope_apply(rms_norm_heads(x, w, heads, eps), f).to(wire_dtype)
+    q = torch.cat([qk(txt[0], wq, txt_freqs), qk(img[0], wq, img_freqs)], 1)
+    k = torch.cat([qk(txt[1], wk, txt_freqs), qk(img[1], wk, img_freqs)], 1)
+    p, d = txt[2].shape[1], txt[2].shape[2] // heads
+    v = torch.cat([txt[2].view(1, p, heads, d), img[2].view(1, -1, heads, d)], 1).to(wire_dtype)
+    out = sdpa_fp32(q, k, v, scale)[0].to(wire_dtype)
+    total = img[0].shape[1]
+    res = []
+    for r in range(world):
+        a, b = shard_bounds(total, r, world)
+        res.append((out[:p], out[p + a:p + b]))
+    return res
 
 
 # ------------------------------------------------------ timed CPU baseline

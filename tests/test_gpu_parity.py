@@ -271,3 +271,161 @@ def test_wan14b_full_size_sampled_rows(cuda_lib, oracle):
         v = xv[..., sl].reshape(1, total, 1, 128)
         ref = oracle.sdpa_fp32(q[:, rows], k, v)[0, :, 0]
         assert_attention_close(out[rows, head], ref)
+
+
+# ------------------------------------------------------- BASELINE config shapes
+def _emulated_block(oracle, x, wq, wk, freqs, total, heads, world):
+    """Run the whole block for every rank of `world` on one GPU (device-side
+    all-to-all emulation); returns per-rank outputs [n_r, H, D] (fp32)."""
+    from powershard_b200 import ops
+    geos = [geometry(total, heads, world, r) for r in range(world)]
+    sends = []
+    for geo in geos:
+        a, b = geo.bounds
+        send = torch.empty(geo.send_shape(), dtype=torch.bfloat16, device=DEV)
+        ops.prepass(*(t[a:b] for t in x), wq, wk, freqs[a:b], send, geo)
+        sends.append(send)
+    outs = []
+    for r, geo in enumerate(geos):
+        recv = torch.stack([sends[s][r] for s in range(world)]).contiguous()
+        o = torch.zeros(geo.out_shape(), dtype=torch.bfloat16, device=DEV)
+        ops.ulysses_attention(recv, o, geo, 128 ** -0.5, None)
+        outs.append(o)
+        del recv
+    del sends
+    results = []
+    for r, geo in enumerate(geos):
+        back = torch.stack([outs[s][r] for s in range(world)]).contiguous()
+        out = torch.empty((geo.n_local, heads, 128), dtype=torch.float32, device=DEV)
+        ops.unpack(back, out, geo)
+        results.append(out)
+    return results
+
+
+def test_config1_wan13b_w2_full(cuda_lib, oracle):
+    """configs[0] shape (Wan2.1-1.3B: L=4096 on a 16x16x16 grid, 12 heads), W=2, every row."""
+    total, heads, grid = 4096, 12, (16, 16, 16)
+    g = torch.Generator().manual_seed(0)
+    x = [(torch.randn(1, total, heads * 128, generator=g) * 1.43).to(torch.bfloat16) for _ in range(3)]
+    w = torch.ones(heads * 128)
+    freqs = oracle.rope_table_3d(grid, 128)
+    outs = _emulated_block(oracle, [t[0].to(DEV) for t in x], w.to(DEV), w.to(DEV), freqs[0, :, 0].to(DEV),
+                           total, heads, 2)
+    expected = oracle.sequence_attention(x[0], x[1], x[2], w, w, freqs, heads, world=2)
+    for r in range(2):
+        assert_attention_close(outs[r], expected[r][0])
+
+
+def _sampled_rows_check(oracle, out_rows_fn, x_cpu, freqs, total, heads, rows, head_ids):
+    ones = torch.ones(heads * 128)
+    q_all = oracle.rms_norm(x_cpu[0][None], ones, 1e-6)
+    k_all = oracle.rms_norm(x_cpu[1][None], ones, 1e-6)
+    for head in head_ids:
+        sl = slice(head * 128, (head + 1) * 128)
+        q = oracle.rope_apply(q_all[..., sl].reshape(1, total, 1, 128), freqs).to(torch.bfloat16)
+        k = oracle.rope_apply(k_all[..., sl].reshape(1, total, 1, 128), freqs).to(torch.bfloat16)
+        v = x_cpu[2][None][..., sl].reshape(1, total, 1, 128)
+        ref = oracle.sdpa_fp32(q[:, rows], k, v)[0, :, 0]
+        assert_attention_close(out_rows_fn(rows, head), ref)
+
+
+def test_config3_ti2v5b_full_size_sampled_rows(cuda_lib, oracle):
+    """configs[2] shape (TI2V-5B: L=27280 on 31x22x40, 24 heads) at W=1."""
+    from powershard_b200.ulysses import UlyssesAttention
+    total, heads, grid = 27280, 24, (31, 22, 40)
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = [torch.randn(total, heads * 128, device=DEV, generator=g, dtype=torch.bfloat16) * 1.43 for _ in range(3)]
+    w = torch.ones(heads * 128, device=DEV)
+    freqs = oracle.rope_table_3d(grid, 128)
+    engine = UlyssesAttention()
+    out = engine.forward(*x, w, w, freqs[0, :, 0].to(DEV), total=total, heads=heads, local=True)
+    engine.check()
+    rows = torch.tensor([0, 5, 127, 128, 9999, 20000, 27135, 27136, 27279])
+    _sampled_rows_check(oracle, lambda r, h: out[r, h], [t.cpu() for t in x], freqs, total, heads, rows, (0, 23))
+
+
+def test_config4_long_75600_w2_sampled_rows(cuda_lib, oracle):
+    """configs[3] shape (L=75600 on 21x45x80, 40 heads) at W=2 (ranks emulated
+    on one GPU): key segments of 37800 rows, > 64K tokens per attention."""
+    total, heads, grid, world = 75600, 40, (21, 45, 80), 2
+    g = torch.Generator(device=DEV).manual_seed(6)
+    x = [torch.randn(total, heads * 128, device=DEV, generator=g, dtype=torch.bfloat16) * 1.43 for _ in range(3)]
+    w = torch.ones(heads * 128, device=DEV)
+    freqs = oracle.rope_table_3d(grid, 128)
+    outs = _emulated_block(oracle, x, w, w, freqs[0, :, 0].to(DEV), total, heads, world)
+    x_cpu = [t.cpu() for t in x]
+    del x
+    n0 = outs[0].shape[0]
+
+    def rows_of(r, h):
+        r = torch.as_tensor(r)
+        return torch.stack([outs[int(i) // n0][int(i) % n0, h] for i in r])
+    rows = torch.tensor([0, 1, 37799, 37800, 50000, 75599])
+    _sampled_rows_check(oracle, rows_of, x_cpu, freqs, total, heads, rows, (0, 21, 39))
+
+
+# --------------------------------------------------- Flux joint (configs[4])
+def _flux_inputs(oracle, txt_len, grid, heads, seed=8):
+    g = torch.Generator().manual_seed(seed)
+    n_img = grid[0] * grid[1]
+    txt = [(torch.randn(1, txt_len, heads * 128, generator=g) * 1.43).to(torch.bfloat16) for _ in range(3)]
+    img = [(torch.randn(1, n_img, heads * 128, generator=g) * 1.43).to(torch.bfloat16) for _ in range(3)]
+    wq = torch.rand(128, generator=g) + 0.5
+    wk = torch.rand(128, generator=g) + 0.5
+    table = oracle.rope_table_flux(txt_len, grid, 128)
+    return txt, img, wq, wk, table[:, :txt_len], table[:, txt_len:]
+
+
+@pytest.mark.parametrize("world,txt_len,grid,heads", [(1, 512, (64, 64), 24), (2, 512, (64, 64), 24),
+                                                      (3, 77, (20, 30), 5), (4, 512, (64, 64), 24)])
+def test_flux_joint_emulated_ranks(cuda_lib, oracle, world, txt_len, grid, heads):
+    """configs[4] (Flux.1-dev: 512 text + 64x64 image tokens, 24 heads): text
+    replicated, image rows Ulysses-split; ranks emulated on one GPU."""
+    from powershard_b200 import ops
+    from powershard_b200.partition import UlyssesGeometry
+    txt, img, wq, wk, tf, imf = _flux_inputs(oracle, txt_len, grid, heads)
+    total = grid[0] * grid[1]
+    expected = oracle.flux_joint_attention(txt, img, wq, wk, tf, imf, heads, world)
+    geos = [geometry(total, heads, world, r) for r in range(world)]
+    tgeo = UlyssesGeometry.replicated(txt_len, heads, 128, world)
+    tsend = torch.empty(tgeo.send_shape(), dtype=torch.bfloat16, device=DEV)
+    ops.prepass(*(t[0].to(DEV) for t in txt), wq.to(DEV), wk.to(DEV), tf[0, :, 0].to(DEV), tsend, tgeo,
+                norm_rope=ops.NORM_PER_HEAD)
+    sends = []
+    for geo in geos:
+        a, b = geo.bounds
+        send = torch.empty(geo.send_shape(), dtype=torch.bfloat16, device=DEV)
+        ops.prepass(*(t[0, a:b].to(DEV) for t in img), wq.to(DEV), wk.to(DEV), imf[0, a:b, 0].to(DEV), send, geo,
+                    norm_rope=ops.NORM_PER_HEAD)
+        sends.append(send)
+    outs, touts = [], []
+    for r, geo in enumerate(geos):
+        recv = torch.stack([sends[s][r] for s in range(world)]).contiguous()
+        o = torch.zeros(geo.out_shape(), dtype=torch.bfloat16, device=DEV)
+        to = torch.zeros((txt_len, geo.heads_per_rank, 128), dtype=torch.bfloat16, device=DEV)
+        ops.ulysses_joint_attention(recv, tsend[r], o, to, geo, 128 ** -0.5, None)
+        outs.append(o)
+        touts.append(to)
+    gathered = torch.stack(touts).contiguous()
+    txt_out = torch.empty((txt_len, heads, 128), dtype=torch.float32, device=DEV)
+    ops.unpack(gathered, txt_out, tgeo)
+    for r, geo in enumerate(geos):
+        back = torch.stack([outs[s][r] for s in range(world)]).contiguous()
+        out = torch.empty((geo.n_local, heads, 128), dtype=torch.float32, device=DEV)
+        ops.unpack(back, out, geo)
+        if geo.n_local:
+            assert_attention_close(out, expected[r][1])
+    assert_attention_close(txt_out, expected[0][0])
+
+
+def test_flux_joint_engine_world1(cuda_lib, oracle):
+    from powershard_b200.ulysses import UlyssesAttention
+    txt, img, wq, wk, tf, imf = _flux_inputs(oracle, 512, (64, 64), 24)
+    engine = UlyssesAttention()
+    t_out, i_out = engine.forward_joint([t[0].to(DEV) for t in txt], [t[0].to(DEV) for t in img], wq.to(DEV),
+                                        wk.to(DEV), tf[0, :, 0].to(DEV), imf[0, :, 0].to(DEV), total_img=4096,
+                                        heads=24)
+    engine.check()
+    expected = oracle.flux_joint_attention(txt, img, wq, wk, tf, imf, 24, 1)
+    assert_attention_close(t_out, expected[0][0])
+    assert_attention_close(i_out, expected[0][1])
