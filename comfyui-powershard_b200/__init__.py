@@ -10,20 +10,24 @@ hand-written CUDA kernels (libps_b200.so, C ABI in include/ps_b200.h):
   buffer in place, all-to-all back, unpack;
 * ``wan.self_attention_forward`` / ``wan.sequence_attention`` - the
   reference's Wan entry points (powershard/wan_model.py:433-502);
+* ``image.SequenceAttention`` - the Flux block attention override
+  (powershard/image_parallel.py:67-110) on the Ulysses exchange and the
+  joint [text; image] kernel;
 * ``probe`` - the provider certification probe (powershard/attention_probe.py).
 
 The package directory doubles as a ComfyUI custom-node folder (it registers
 no nodes; PowerShard selects the provider by ``attention_backend="b200"``).
 """
 from .contract import AttentionOptions, UnsupportedAttention, validate
-from .partition import UlyssesGeometry, shard_bounds
+from .partition import ImageLayout, UlyssesGeometry, shard_bounds, split_sizes
 
 NODE_CLASS_MAPPINGS: dict = {}
 NODE_DISPLAY_NAME_MAPPINGS: dict = {}
 
 __all__ = [
     "AttentionOptions", "UnsupportedAttention", "validate", "UlyssesGeometry", "shard_bounds",
-    "B200Provider", "UlyssesAttention", "NODE_CLASS_MAPPINGS", "NODE_DISPLAY_NAME_MAPPINGS",
+    "ImageLayout", "split_sizes", "B200Provider", "UlyssesAttention", "SequenceAttention",
+    "NODE_CLASS_MAPPINGS", "NODE_DISPLAY_NAME_MAPPINGS",
 ]
 
 
@@ -34,4 +38,7 @@ def __getattr__(name):  # lazy: importing the package never needs a GPU
     if name == "UlyssesAttention":
         from .ulysses import UlyssesAttention
         return UlyssesAttention
+    if name == "SequenceAttention":
+        from .image import SequenceAttention
+        return SequenceAttention
     raise AttributeError(name)

@@ -26,7 +26,7 @@ SIGNATURES = {
     "ps_b200_abi_version": (ctypes.c_int, []),
     "ps_b200_last_error": (ctypes.c_char_p, []),
     "ps_b200_prepass": (ctypes.c_int, [
-        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, _c_i64p,
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64,
         ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
@@ -37,8 +37,8 @@ SIGNATURES = {
         ctypes.c_int, ctypes.c_int, ctypes.c_float, _c_intp, ctypes.c_void_p]),
     "ps_b200_ulysses_attn_fwd": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _c_intp,
-        ctypes.c_void_p]),
+        ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+        _c_intp, ctypes.c_void_p]),
     "ps_b200_block_fwd_static": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
@@ -47,8 +47,8 @@ SIGNATURES = {
     "ps_b200_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "ps_b200_ulysses_joint_attn_fwd": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_float, _c_intp, ctypes.c_void_p]),
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_float, _c_intp, ctypes.c_void_p]),
     "ps_b200_unpack": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
@@ -110,6 +110,14 @@ def dtype_code(dtype: torch.dtype) -> int:
     if dtype == torch.float32:
         return FP32
     raise UnsupportedAttention(f"dtype {dtype} is not supported by the b200 kernels")
+
+
+def i32(values):
+    """ctypes int array of `values` (None stays None)."""
+    if values is None:
+        return None
+    values = [int(v) for v in values]
+    return (ctypes.c_int * len(values))(*values)
 
 
 def i64(values):

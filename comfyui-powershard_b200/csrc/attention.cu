@@ -94,21 +94,9 @@ enum Err : int {
   kErrDrain = 107,
 };
 
-__device__ __forceinline__ void tile_coord(int t, int full_segs, int tiles_per_seg, int seg_rows,
-                                           int len, int& seg, int& row0, int& valid) {
-  if (t < full_segs * tiles_per_seg) {
-    seg = t / tiles_per_seg;
-    row0 = (t - seg * tiles_per_seg) * kBlockM;
-    valid = min(kBlockM, seg_rows - row0);
-  } else {
-    seg = full_segs;
-    row0 = (t - full_segs * tiles_per_seg) * kBlockM;
-    valid = min(kBlockM, len - full_segs * seg_rows - row0);
-  }
-}
-
-// Walks the key tiles - the prefix range first, then (segment, first row)
-// of the segmented range - returning the valid rows of each, without divisions.
+// Walks the key tiles - the prefix range first, then the segmented range
+// segment by segment (skipping empty segments) - returning each tile's
+// segment, first row and valid rows, without divisions.
 struct KeyCursor {
   int i = 0, seg = 0, row0 = 0;
   __device__ __forceinline__ void next(const AttnArgs& a, bool& prefix, int& s, int& r, int& valid) {
@@ -122,19 +110,19 @@ struct KeyCursor {
     }
     ++i;
     prefix = false;
-    const int seg_len = seg < a.kv_full_segs ? a.seg_rows_k : a.len_k - a.kv_full_segs * a.seg_rows_k;
-    s = seg;
-    r = row0;
-    valid = min(kBlockN, seg_len - row0);
-    row0 += kBlockN;
-    if (row0 >= seg_len) {
+    while (row0 >= a.valid_k[seg] && seg + 1 < a.nsegs_k) {
       ++seg;
       row0 = 0;
     }
+    s = seg;
+    r = row0;
+    valid = min(kBlockN, a.valid_k[seg] - row0);
+    row0 += kBlockN;
   }
 };
 
-// Query tile t: prefix tiles first, then the segmented range.
+// Query tile t: prefix tiles first, then q_tiles_per_seg tiles per segment
+// (a tile past its segment's valid rows has valid <= 0 and is never stored).
 __device__ __forceinline__ void q_tile(const AttnArgs& a, int t, bool& prefix, int& seg, int& row0, int& valid) {
   if (t < a.pre_tiles) {
     prefix = true;
@@ -143,7 +131,10 @@ __device__ __forceinline__ void q_tile(const AttnArgs& a, int t, bool& prefix, i
     valid = min(kBlockM, a.pre_len - row0);
   } else {
     prefix = false;
-    tile_coord(t - a.pre_tiles, a.q_full_segs, a.q_tiles_per_seg, a.seg_rows_q, a.len_q, seg, row0, valid);
+    const int u = t - a.pre_tiles;
+    seg = u / a.q_tiles_per_seg;
+    row0 = (u - seg * a.q_tiles_per_seg) * kBlockM;
+    valid = min(kBlockM, a.valid_q[seg] - row0);
   }
 }
 

@@ -81,11 +81,28 @@ int make_map(CUtensorMap* m, const void* base, bool fp16, int head_dim, int head
   return PS_B200_OK;
 }
 
-void tile_plan(int seg_rows, int len, int& full_segs, int& tiles_per_seg, int& num_tiles) {
-  full_segs = len / seg_rows;
-  tiles_per_seg = (seg_rows + 127) / 128;
-  const int rem = len - full_segs * seg_rows;
-  num_tiles = full_segs * tiles_per_seg + (rem + 127) / 128;
+// An explicit per-segment row table must have world entries in [0, seg_rows]
+// summing to total.
+int check_seg_valid(const int* seg_valid, int world, int seg_rows, int total) {
+  if (!seg_valid) return PS_B200_OK;
+  if (world > kMaxSegs) return set_error(PS_B200_ERR_UNSUPPORTED, "more than %d segments", kMaxSegs);
+  int64_t sum = 0;
+  for (int s = 0; s < world; ++s) {
+    if (seg_valid[s] < 0 || seg_valid[s] > seg_rows)
+      return set_error(PS_B200_ERR_INVALID, "segment %d holds %d rows, outside [0, %d]", s, seg_valid[s], seg_rows);
+    sum += seg_valid[s];
+  }
+  if (sum != total) return set_error(PS_B200_ERR_INVALID, "segment rows sum to %lld, not total %d", (long long)sum, total);
+  return PS_B200_OK;
+}
+
+// Valid rows per segment when `len` rows fill segments of `seg_rows` in order
+// (ceil-width token shards: only the last non-empty segment is short).
+void fill_valid(int* valid, int segs, int seg_rows, int len) {
+  for (int s = 0; s < segs; ++s) {
+    const int64_t v = int64_t(len) - int64_t(s) * seg_rows;
+    valid[s] = int(v < 0 ? 0 : (v > seg_rows ? seg_rows : v));
+  }
 }
 
 struct SegTensor {
@@ -107,8 +124,11 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
                      const int64_t out_st[4], int dtype, int out_dtype, int batch, int grid_heads, int group,
                      int head_dim,
                      int seg_rows_q, int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k,
-                     float softmax_scale, int* status, void* stream, const Prefix* pre = nullptr) {
+                     float softmax_scale, int* status, void* stream, const Prefix* pre = nullptr,
+                     const int* seg_valid = nullptr) {
   const int pre_len = pre ? pre->len : 0;
+  if (segs_q > kMaxSegs || segs_k > kMaxSegs)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "more than %d segments", kMaxSegs);
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "attention supports bf16 and fp16 only");
   if (out_dtype != dtype && out_dtype != PS_B200_FP32)
     return set_error(PS_B200_ERR_UNSUPPORTED, "attention output must be fp32 or the input dtype");
@@ -157,11 +177,27 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
   a.out = out;
   for (int i = 0; i < 4; ++i) a.o_stride[i] = out_st[i];
   a.seg_rows_q = seg_rows_q;
-  a.len_q = len_q;
-  tile_plan(seg_rows_q, len_q, a.q_full_segs, a.q_tiles_per_seg, a.num_q_tiles);
+  a.nsegs_q = segs_q;
+  a.q_tiles_per_seg = (seg_rows_q + 127) / 128;
   a.seg_rows_k = seg_rows_k;
-  a.len_k = len_k;
-  tile_plan(seg_rows_k, len_k, a.kv_full_segs, a.kv_tiles_per_seg, a.num_kv_tiles);
+  a.nsegs_k = segs_k;
+  if (seg_valid) {  // explicit per-segment rows (queries and keys share the segments)
+    for (int s = 0; s < segs_q; ++s) {
+      if (seg_valid[s] < 0 || seg_valid[s] > seg_rows_q)
+        return set_error(PS_B200_ERR_INVALID, "segment %d valid rows %d outside [0, %d]", s, seg_valid[s], seg_rows_q);
+      a.valid_q[s] = a.valid_k[s] = seg_valid[s];
+    }
+  } else {
+    fill_valid(a.valid_q, segs_q, seg_rows_q, len_q);
+    fill_valid(a.valid_k, segs_k, seg_rows_k, len_k);
+  }
+  // Query tiles are laid out segment-major (tiles past a segment's valid rows
+  // compute on padding and store nothing); trailing empty segments are dropped.
+  int last_q = segs_q - 1;
+  while (last_q >= 0 && a.valid_q[last_q] == 0) --last_q;
+  a.num_q_tiles = (last_q + 1) * a.q_tiles_per_seg;
+  a.num_kv_tiles = 0;
+  for (int s = 0; s < segs_k; ++s) a.num_kv_tiles += (a.valid_k[s] + 127) / 128;
   a.group = group;
   a.scale_log2 = static_cast<float>(double(softmax_scale) * 1.4426950408889634);
   a.out_fp32 = out_dtype == PS_B200_FP32;
@@ -200,8 +236,8 @@ int ps_b200_abi_version(void) { return PS_B200_ABI_VERSION; }
 const char* ps_b200_last_error(void) { return psb::g_msg; }
 
 int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
-                    const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,
-                    int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
+                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
                     int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
   if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
@@ -218,8 +254,10 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   if (n_local > 0) {
     const void* xs[3] = {x_q, x_k, x_v};
     for (int i = 0; i < 3; ++i)
-      if (!xs[i] || !aligned16(xs[i]) || !x_row_strides || x_row_strides[i] % 8 != 0 || x_row_strides[i] < 0)
-        return set_error(PS_B200_ERR_INVALID, "projection inputs must be 16-byte aligned with row strides %% 8 == 0");
+      if (!xs[i] || !aligned16(xs[i]) || !x_row_strides || x_row_strides[i] % 8 != 0 || x_row_strides[i] < 0 ||
+          (x_head_strides && (x_head_strides[i] % 8 != 0 || x_head_strides[i] < 0)))
+        return set_error(PS_B200_ERR_INVALID,
+                         "projection inputs must be 16-byte aligned with row and head strides %% 8 == 0");
     if (norm_rope) {
       if (!w_qnorm || !w_knorm || !aligned16(w_qnorm) || !aligned16(w_knorm))
         return set_error(PS_B200_ERR_INVALID, "norm weights null or not 16-byte aligned");
@@ -235,7 +273,10 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   a.x[0] = x_q;
   a.x[1] = x_k;
   a.x[2] = x_v;
-  for (int i = 0; i < 3; ++i) a.x_row_stride[i] = x_row_strides ? x_row_strides[i] : 0;
+  for (int i = 0; i < 3; ++i) {
+    a.x_row_stride[i] = x_row_strides ? x_row_strides[i] : 0;
+    a.x_head_stride[i] = x_head_strides ? x_head_strides[i] : head_dim;
+  }
   a.w[0] = w_qnorm;
   a.w[1] = w_knorm;
   a.w_fp32 = w_dtype == PS_B200_FP32;
@@ -269,11 +310,12 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
 }
 
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
-                             int total, int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
-                             int* status, void* stream) {
+                             int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                             float softmax_scale, int* status, void* stream) {
   if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
       heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
     return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
+  if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
   if (total == 0 || heads_valid == 0) return PS_B200_OK;
   const int64_t D = head_dim, h = heads_per_rank, n = seg_rows;
   const int64_t block = n * h * D;  // one [seg_rows][h][D] block
@@ -284,16 +326,17 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
   SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows, world, total,
-                          seg_rows, world, total, softmax_scale, status, stream);
+                          seg_rows, world, total, softmax_scale, status, stream, nullptr, seg_valid);
 }
 
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
                                    int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
-                                   int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
-                                   int* status, void* stream) {
+                                   const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                                   float softmax_scale, int* status, void* stream) {
   if (world < 1 || seg_rows < 1 || total < 1 || prefix_len < 0 || heads_per_rank < 1 || heads_valid < 0 ||
       heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
     return set_error(PS_B200_ERR_INVALID, "inconsistent joint Ulysses geometry");
+  if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
   if (heads_valid == 0) return PS_B200_OK;
   const int64_t D = head_dim, h = heads_per_rank, n = seg_rows, P = prefix_len;
   const int64_t block = n * h * D;
@@ -319,7 +362,7 @@ int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, voi
     pre.out_st[3] = D;
   }
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
-                          world, total, seg_rows, world, total, softmax_scale, status, stream, &pre);
+                          world, total, seg_rows, world, total, softmax_scale, status, stream, &pre, seg_valid);
 }
 
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,

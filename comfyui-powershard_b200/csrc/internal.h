@@ -7,20 +7,21 @@
 
 namespace psb {
 
+constexpr int kMaxSegs = 64;  // segments (source ranks) per attention call
+
 // Arguments of the attention kernel that are not tensor maps.
 struct AttnArgs {
   void* out;             // output element (batch 0, seg 0, row 0, head 0, d 0)
   int64_t o_stride[4];   // batch, segment, row, head strides in elements (d stride 1)
-  int seg_rows_q;        // rows per query segment
-  int len_q;             // valid query rows over all segments
-  int q_full_segs;       // len_q / seg_rows_q
+  int seg_rows_q;        // rows allocated per query segment
+  int nsegs_q;           // query segments
   int q_tiles_per_seg;   // ceil(seg_rows_q / 128)
-  int num_q_tiles;       // query tiles with at least one valid row
+  int num_q_tiles;       // prefix tiles + nsegs_q * q_tiles_per_seg
   int seg_rows_k;
-  int len_k;
-  int kv_full_segs;
-  int kv_tiles_per_seg;
-  int num_kv_tiles;
+  int nsegs_k;
+  int num_kv_tiles;      // prefix tiles + sum over key segments of ceil(valid_k / 128)
+  int valid_q[kMaxSegs]; // valid rows of each query segment (a prefix of its rows)
+  int valid_k[kMaxSegs];
   int group;             // query heads per key/value head (GQA)
   float scale_log2;      // softmax_scale * log2(e)
   int out_fp32;          // 1: output fp32, 0: output in the input 16-bit type
@@ -41,6 +42,7 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 struct PrepassArgs {
   const void* x[3];        // q, k, v projection outputs, [n_local][heads*head_dim]
   int64_t x_row_stride[3]; // elements between consecutive tokens
+  int64_t x_head_stride[3];// elements between consecutive heads of a token (head_dim: [n][H*D] rows)
   const void* w[2];        // RMSNorm weights of q and k, [heads*head_dim]
   int w_fp32;              // 1: weights are fp32, 0: same 16-bit type as x
   const float* freqs;      // [n_local][head_dim/2][2][2] fp32

@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
       const int v = tid + u * kThreads;
       ss[u] = 0.f;
       if (v < nvec) {
-        xv[u] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(v) * 8));
+        const int g = v / vph;
+        xv[u] = __ldg(reinterpret_cast<const uint4*>(x + g * a.x_head_stride[kind] + (v - g * vph) * 8));
         if (normed) {
           uint16_t e[8];
           unpack8(xv[u], e);

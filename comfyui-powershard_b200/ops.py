@@ -64,9 +64,11 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
             norm_rope=True):
     """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
 
-    x_*: [n_local, H*D] (row stride may exceed H*D); freqs: [n_local, D/2, 2, 2]
-    fp32.  norm_rope: False/0 pack only, True/1 RMSNorm over the full width
-    (Wan; w_* [H*D]), 2 RMSNorm per head (Flux QK-norm; w_* [D]).
+    x_*: [n_local, H*D] (row stride may exceed H*D) or [n_local, H, D] with
+    any row and head strides (e.g. a [H, L, D] tensor transposed) and unit
+    inner stride; freqs: [n_local, D/2, 2, 2] fp32.  norm_rope: False/0 pack
+    only, True/1 RMSNorm over the full width (Wan; w_* [H*D]), 2 RMSNorm per
+    head (Flux QK-norm; w_* [D]).
     """
     mode = int(norm_rope)
     lib = _lib.load()
@@ -74,10 +76,15 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
         _check16(t, f"prepass {name}")
     n = geo.n_local
     width = geo.heads * geo.head_dim
+    head_strides = []
     for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v")):
-        if t.dim() != 2 or t.shape[0] != n or t.shape[1] != width or t.stride(1) != 1:
-            raise ValueError(f"prepass {name}: expected [{n}, {width}] with unit inner stride, got "
-                             f"{tuple(t.shape)} / {t.stride()}")
+        if t.dim() == 3 and tuple(t.shape) == (n, geo.heads, geo.head_dim) and t.stride(2) == 1:
+            head_strides.append(t.stride(1))
+        elif t.dim() == 2 and t.shape[0] == n and t.shape[1] == width and t.stride(1) == 1:
+            head_strides.append(geo.head_dim)
+        else:
+            raise ValueError(f"prepass {name}: expected [{n}, {width}] or [{n}, {geo.heads}, {geo.head_dim}] "
+                             f"with unit inner stride, got {tuple(t.shape)} / {t.stride()}")
         if t.dtype != send.dtype:
             raise ValueError("prepass: q/k/v and send dtypes differ")
     if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
@@ -102,11 +109,16 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
         fptr, fstride = freqs.data_ptr(), freqs.stride(0)
     rc = lib.ps_b200_prepass(
         x_q.data_ptr(), x_k.data_ptr(), x_v.data_ptr(),
-        _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]),
+        _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]), _lib.i64(head_strides),
         wq, wk, w_dtype, fptr, fstride, send.data_ptr(), _lib.dtype_code(send.dtype),
         geo.world, n, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
         mode, _lib.stream_handle(send.device))
     _lib.check(rc, "ps_b200_prepass")
+
+
+def _seg_table(geo: UlyssesGeometry):
+    """Per-segment row table for the C ABI: None for ceil-width shards."""
+    return _lib.i32(geo.sizes) if geo.sizes is not None else None
 
 
 def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status: DeviceStatus | None):
@@ -122,7 +134,8 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
         raise ValueError("attention: output dtype must be fp32 or the input dtype")
     rc = lib.ps_b200_ulysses_attn_fwd(
         recv.data_ptr(), out_send.data_ptr(), _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype),
-        geo.world, geo.width, geo.total, geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale),
+        geo.world, geo.width, geo.total, _seg_table(geo), geo.heads_per_rank, geo.heads_valid, geo.head_dim,
+        float(scale),
         status.ptr if status is not None else None, _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_attn_fwd")
     if status is not None:
@@ -152,7 +165,7 @@ def ulysses_joint_attention(recv, prefix_qkv, out_send, prefix_out, geo: Ulysses
     rc = lib.ps_b200_ulysses_joint_attn_fwd(
         recv.data_ptr(), prefix_qkv.data_ptr(), out_send.data_ptr(), prefix_out.data_ptr(),
         _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype), geo.world, geo.width, geo.total, plen,
-        h, geo.heads_valid, d, float(scale), status.ptr if status is not None else None,
+        _seg_table(geo), h, geo.heads_valid, d, float(scale), status.ptr if status is not None else None,
         _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_joint_attn_fwd")
     if status is not None:

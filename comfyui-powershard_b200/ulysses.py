@@ -50,9 +50,13 @@ class UlyssesAttention:
             return dist.get_world_size(self.group), dist.get_rank(self.group)
         return 1, 0
 
-    def geometry(self, total: int, heads: int, head_dim: int, local: bool = False) -> UlyssesGeometry:
+    def geometry(self, total: int, heads: int, head_dim: int, local: bool = False,
+                 sizes=None) -> UlyssesGeometry:
         world, rank = (1, 0) if local else self.world_rank()
-        return UlyssesGeometry(total=total, heads=heads, head_dim=head_dim, world=world, rank=rank)
+        if sizes is not None and len(sizes) != world:
+            raise ValueError(f"{len(sizes)} split sizes for a group of {world} ranks")
+        return UlyssesGeometry(total=total, heads=heads, head_dim=head_dim, world=world, rank=rank,
+                               sizes=None if sizes is None else tuple(sizes))
 
     # ------------------------------------------------------------ buffers
     def _workspace(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
@@ -118,24 +122,30 @@ class UlyssesAttention:
             state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
         return out
 
-    def forward_joint(self, txt, img, w_q, w_k, txt_freqs, img_freqs, *, total_img: int, heads: int,
-                      eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
-                      norm: int = ops.NORM_PER_HEAD, state: dict | None = None):
+    def forward_joint(self, txt, img, w_q=None, w_k=None, txt_freqs=None, img_freqs=None, *, total_img: int,
+                      heads: int, eps: float = 1e-6, scale: float | None = None,
+                      out_dtype: torch.dtype | None = None, norm: int = ops.NORM_PER_HEAD,
+                      state: dict | None = None, sizes=None, out=None):
         """Flux joint attention: text rows replicated on every rank, image rows Ulysses-split.
 
-        txt = (q, k, v) [P, H*D] projections of the P text tokens (identical on
-        every rank); img = (q, k, v) [n_img_local, H*D] of this rank's image
-        tokens (shard_bounds of total_img); txt_freqs [P, D/2, 2, 2] and
-        img_freqs [n_img_local, D/2, 2, 2].  Keys and queries of every head
-        are [text; all image tokens].  Only image rows cross the all-to-all;
-        each rank attends text queries for its own heads and the text outputs
-        are all-gathered over heads.  Returns (txt_out [P, H, D],
-        img_out [n_img_local, H, D]) in out_dtype.
+        txt = (q, k, v) [P, H*D] (or [P, H, D], any row/head strides)
+        projections of the P text tokens (identical on every rank); img =
+        (q, k, v) [n_img_local, H*D] of this rank's image tokens: the
+        shard_bounds part of total_img, or part `rank` of `sizes` (the image
+        Layout's balanced split).  With norm NORM_PER_HEAD, w_q/w_k [D] are
+        the QK-norm weights and txt_freqs [P, D/2, 2, 2] / img_freqs
+        [n_img_local, D/2, 2, 2] the rotation tables; with NORM_NONE the
+        inputs are already normalised/rotated and only exchanged.  Keys and
+        queries of every head are [text; all image tokens].  Only image rows
+        cross the all-to-all; each rank attends text queries for its own
+        heads and the text outputs are all-gathered over heads.  Returns
+        (txt_out [P, H, D], img_out [n_img_local, H, D]) in out_dtype, written
+        into `out` = (txt_out, img_out) when given (contiguous tensors).
         """
         device = img[0].device
         dtype = img[0].dtype
-        head_dim = img[0].shape[-1] // heads
-        geo = self.geometry(total_img, heads, head_dim)
+        head_dim = img[0].shape[-1] if img[0].dim() == 3 else img[0].shape[-1] // heads
+        geo = self.geometry(total_img, heads, head_dim, sizes=sizes)
         if img[0].shape[0] != geo.n_local:
             raise ValueError("Ulysses local token/head geometry mismatch")
         plen = txt[0].shape[0]
@@ -150,11 +160,21 @@ class UlyssesAttention:
             if tkey not in self._buffers:  # text rows: packed q/k/v and this rank's heads' outputs (wire dtype)
                 self._buffers[tkey] = dict(
                     send=torch.empty(tgeo.send_shape(), dtype=dtype, device=device),
-                    out=torch.empty((plen, geo.heads_per_rank, head_dim), dtype=dtype, device=device))
+                    out=torch.empty((plen, geo.heads_per_rank, head_dim), dtype=dtype, device=device),
+                    gathered=torch.empty((geo.world * plen, geo.heads_per_rank, head_dim), dtype=dtype,
+                                         device=device))  # concatenated along dim 0 (any backend)
             tb = self._buffers[tkey]
-            img_out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
-            txt_out = torch.empty((plen, heads, head_dim), dtype=out_dtype, device=device)
-            k.prepass(*txt, w_q, w_k, txt_freqs, tb["send"], tgeo, eps, norm)
+            if out is not None:
+                txt_out, img_out = out
+                for t, rows in ((txt_out, plen), (img_out, geo.n_local)):
+                    if tuple(t.shape) != (rows, heads, head_dim) or not t.is_contiguous() or t.dtype != out_dtype:
+                        raise ValueError(f"forward_joint: out tensors must be contiguous [{rows}, {heads}, "
+                                         f"{head_dim}] {out_dtype}")
+            else:
+                img_out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
+                txt_out = torch.empty((plen, heads, head_dim), dtype=out_dtype, device=device)
+            if plen:
+                k.prepass(*txt, w_q, w_k, txt_freqs, tb["send"], tgeo, eps, norm)
             k.prepass(*img, w_q, w_k, img_freqs, ws["send"], geo, eps, norm)
             self._exchange(ws["recv"], ws["send"], geo)
             prefix = tb["send"][geo.rank]
@@ -165,9 +185,9 @@ class UlyssesAttention:
                 k.ulysses_joint_attention(ws["recv"], prefix, ws["out_send"], tb["out"], geo, scale, status)
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
                 k.unpack(ws["out_recv"], img_out, geo)
-                gathered = torch.empty((geo.world,) + tuple(tb["out"].shape), dtype=dtype, device=device)
-                dist.all_gather_into_tensor(gathered, tb["out"], group=self.group)
-                k.unpack(gathered, txt_out, tgeo)
+                if plen:
+                    dist.all_gather_into_tensor(tb["gathered"], tb["out"], group=self.group)
+                    k.unpack(tb["gathered"].view(tgeo.out_shape()), txt_out, tgeo)
         if state is not None:
             qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
             state["padded_heads"] = geo.padded_heads

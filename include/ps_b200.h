@@ -66,8 +66,12 @@ const char* ps_b200_last_error(void);
 /*
  * Fused q/k RMSNorm + RoPE + Ulysses pack (replaces attention_qkv plus the
  * send-side packing of ulysses_to_sequence).
- *   x_q, x_k, x_v  [n_local][heads*head_dim] projection outputs (dtype), row
- *                  strides x_row_strides[0..2] in elements (16-byte aligned).
+ *   x_q, x_k, x_v  [n_local][heads][head_dim] projection outputs (dtype), row
+ *                  strides x_row_strides[0..2] and head strides
+ *                  x_head_strides[0..2] in elements (multiples of 8; NULL
+ *                  head strides = head_dim, i.e. [n_local][heads*head_dim]
+ *                  rows; head stride L*head_dim reads a [heads][L][head_dim]
+ *                  tensor, ComfyUI's skip_reshape layout).
  *   w_qnorm, w_knorm RMSNorm weights, w_dtype = dtype or FP32: [heads*head_dim]
  *                  for norm_rope 1, [head_dim] (shared by all heads) for 2.
  *   freqs          [n_local][head_dim/2][2][2] fp32 rotation table (the
@@ -79,8 +83,8 @@ const char* ps_b200_last_error(void);
  * send buffer are written as zeros.
  */
 int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
-                    const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,
-                    int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
+                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
                     int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream);
 
 /*
@@ -103,11 +107,18 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
  * result goes to out_send [world][seg_rows][heads_per_rank][head_dim], the
  * send buffer of the inverse all-to-all (rows >= the destination's valid
  * rows and heads >= heads_valid are left untouched).  out_dtype = dtype or
- * FP32 (then out_send holds fp32 elements).
+ * FP32 (then out_send holds fp32 elements).  seg_valid: host array of
+ * `world` ints, the valid rows of each source segment (at most seg_rows each,
+ * summing to total; at most 64 segments), or NULL for ceil-width token shards
+ * (segment s holds min(seg_rows, max(0, total - s*seg_rows)) rows, the
+ * split of shard_bounds, powershard/config.py:107-112).  An explicit table
+ * serves the balanced split of the image Layout
+ * (powershard/image_layout.py:12-15), whose padding rows may sit in middle
+ * segments.
  */
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
-                             int total, int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
-                             int* status, void* stream);
+                             int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                             float softmax_scale, int* status, void* stream);
 
 /*
  * Joint attention (Flux: text tokens replicated on every rank, image tokens
@@ -115,14 +126,16 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
  * [3][prefix_len][heads_per_rank][head_dim] followed by the image rows of the
  * receive buffer recv (as in ps_b200_ulysses_attn_fwd).  Text query outputs
  * go to prefix_out [prefix_len][heads_per_rank][head_dim], image query
- * outputs to out_send.  No counterpart call in the reference, which
+ * outputs to out_send.  seg_valid as in ps_b200_ulysses_attn_fwd (the
+ * image Layout's balanced split, or NULL for ceil-width shards).  No
+ * counterpart call in the reference, which
  * all-gathers K/V for this model (powershard/image_parallel.py:96-110); the
  * result equals attention over [text; image] (ComfyUI Flux joint attention).
  */
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
                                    int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
-                                   int heads_per_rank, int heads_valid, int head_dim, float softmax_scale,
-                                   int* status, void* stream);
+                                   const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                                   float softmax_scale, int* status, void* stream);
 
 /*
  * Inverse unpack: recv [world][seg_rows][heads_per_rank][head_dim] (dtype)

@@ -10,7 +10,8 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its
 Parity pinning: ``tests/golden/make_golden.py`` imported the reference
 package from its source tree and recorded its outputs (RMSNorm, rope_apply,
 attention_qkv, ulysses_to_sequence / ulysses_to_heads over emulated
-collectives, math_attention, sequence_attention) as fixtures under
+collectives, math_attention, sequence_attention, image_parallel's
+SequenceAttention over an image_layout.Layout) as fixtures under
 ``tests/golden/``; ``tests/test_oracle_golden.py`` checks every function here
 against them.  One piece is NOT pinned: the 3-D RoPE *table*
 (``rope_table_3d``) restates ComfyUI's ``WanModel.rope_encode`` (ComfyUI sha
@@ -31,7 +32,8 @@ __all__ = [
     "shard_bounds", "rms_norm", "rope_apply", "rope_axes", "rope_table_3d",
     "rope_table_flux", "attention_qkv", "pack_qkv", "exchange", "unpack_qkv",
     "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention",
-    "rms_norm_heads", "flux_joint_attention", "time_reference_sample",
+    "rms_norm_heads", "flux_joint_attention", "split_sizes", "image_local_ranges",
+    "image_sequence_attention", "time_reference_sample",
 ]
 
 
@@ -327,6 +329,52 @@ def flux_joint_attention(txt, img, wq, wk, txt_freqs, img_freqs, heads: int, wor
     for r in range(world):
         a, b = shard_bounds(total, r, world)
         res.append((out[:p], out[p + a:p + b]))
+    return res
+
+
+# ------------------------------------- image Layout sequence attention
+def split_sizes(n: int, world: int):
+    """Balanced split of n rows: the first n % world ranks get one extra row
+    (powershard/image_layout.py:12-15)."""
+    base, extra = divmod(int(n), int(world))
+    return [base + (1 if r < extra else 0) for r in range(int(world))]
+
+
+def image_local_ranges(segments, world: int, rank: int):
+    """Global row ranges that make up `rank`'s local sequence for segments
+    [(rows, split)] with exactly one split segment: all rows before the split
+    segment, the rank's part [a, b) of its balanced split, all rows after it
+    (powershard/image_layout.py:22-49)."""
+    total = sum(int(n) for n, _ in segments)
+    start = 0
+    for n, split in segments:
+        if split:
+            split_start, split_len = start, int(n)
+        start += int(n)
+    sizes = split_sizes(split_len, world)
+    a = split_start + sum(sizes[:rank])
+    b = a + sizes[rank]
+    out = []
+    if split_start > 0:
+        out.append((0, split_start))
+    if b > a:
+        out.append((a, b))
+    if split_start + split_len < total:
+        out.append((split_start + split_len, total))
+    return out
+
+
+def image_sequence_attention(q, k, v, segments, world: int, scale=None):
+    """What powershard/image_parallel.py:96-110 (SequenceAttention.__call__)
+    returns on every rank: the rank's local query rows (image_local_ranges)
+    attend over the full key/value sequence that assemble_full (:45-52)
+    rebuilds by all-gathering the split segment.  q, k, v: full [B, L, H, D];
+    returns per rank the fp32 output [B, n_local, H, D] of those rows."""
+    out = sdpa_fp32(q, k, v, scale)
+    res = []
+    for r in range(world):
+        rows = [i for s, e in image_local_ranges(segments, world, r) for i in range(s, e)]
+        res.append(out[:, rows])
     return res
 
 

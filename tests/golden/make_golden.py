@@ -19,6 +19,10 @@ inputs + outputs with torch.save next to this script:
 * ``math_attention.pt`` - attention_contract.math_attention cases.
 * ``sequence_attention.pt`` - wan_model.sequence_attention (Ulysses, math
   provider, fp32 wire) for W in {1,2,3} on a 40-token, 5-head, D=128 layer.
+* ``image_sequence_attention.pt`` - image_parallel.SequenceAttention (the
+  Flux/Qwen attention override: local queries, all-gathered keys/values)
+  over image_layout.Layout for uneven image segments, W in {2,3,5}, with a
+  dense fp32 stand-in for ComfyUI's optimized_attention as `func`.
 
 Collectives are emulated in-process with one thread per rank (the same
 technique as the reference's test_ulysses_tensor_permutation_reference).
@@ -47,7 +51,7 @@ def emulated_collectives(world):
     barrier = threading.Barrier(world, timeout=60)
     slots = [None] * world
     saved = {n: getattr(dist, n) for n in ("get_world_size", "get_rank", "all_to_all_single",
-                                           "all_gather_into_tensor", "all_reduce")}
+                                           "all_gather_into_tensor", "all_reduce", "get_backend")}
 
     def all_to_all(output, input, group=None):
         slots[local.rank] = input.clone()
@@ -72,6 +76,7 @@ def emulated_collectives(world):
     dist.all_to_all_single = all_to_all
     dist.all_gather_into_tensor = all_gather
     dist.all_reduce = all_reduce
+    dist.get_backend = lambda group=None: "nccl"  # selects all_gather_into_tensor in image_parallel
 
     def run(fn):
         def worker(rank):
@@ -210,6 +215,46 @@ def main():
         scases.append(dict(world=world, heads=heads, total=n_total, dim=dim, ranks=per_rank))
     torch.save(dict(q_lin=q_lin, k_lin=k_lin, v_lin=v_lin, wq=wq, wk=wk, freqs=freqs, eps=1e-6,
                     cases=scases), HERE / "sequence_attention.pt")
+    # ---------------------------------------- image Layout SequenceAttention
+    from powershard import image_parallel
+    from powershard.image_layout import Layout
+
+    def dense(q, k, v, heads, mask=None, skip_reshape=False, **kwargs):
+        """Stand-in for ComfyUI optimized_attention: q/k/v [B,H,L,D] with
+        skip_reshape, else [B,L,H*D]; returns [B,Lq,H*D] (fp32 math)."""
+        if not skip_reshape:
+            b, _, width = q.shape
+            q, k, v = (t.view(b, -1, heads, width // heads).transpose(1, 2) for t in (q, k, v))
+        o = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+        return o.transpose(1, 2).reshape(o.shape[0], o.shape[2], -1).to(q.dtype)
+
+    icases = []
+    for segments, world, batch, skip in (([(5, False), (13, True)], 2, 1, True),
+                                         ([(5, False), (13, True)], 3, 2, False),
+                                         ([(5, False), (13, True)], 5, 1, True),
+                                         ([(4, False), (11, True), (3, False)], 3, 1, True)):
+        heads, dim = 3, 16
+        total = sum(n for n, _ in segments)
+        gen = torch.Generator().manual_seed(31 + world)
+        q, k, v = (torch.randn(batch, heads, total, dim, generator=gen) for _ in range(3))
+
+        def rank_fn(rank):
+            lay = Layout(segments, world, rank)
+            stats = {}
+            local = [image_parallel.localize(t, lay, 2) for t in (q, k, v)]
+            if not skip:
+                local = [t.transpose(1, 2).reshape(batch, t.shape[2], heads * dim) for t in local]
+            sa = image_parallel.SequenceAttention(lay, stats)
+            with torch.no_grad():
+                out = sa(dense, *local, heads, skip_reshape=skip)
+            return dict(out=out, sizes=list(lay.sizes), local_ranges=lay.local_ranges(), local_len=lay.local_len,
+                        chunk=lay.chunk, stats=dict(stats))
+        with emulated_collectives(world) as run:
+            per_rank = run(rank_fn)
+        icases.append(dict(segments=segments, world=world, heads=heads, skip_reshape=skip, q=q, k=k, v=v,
+                           ranks=per_rank))
+    torch.save(icases, HERE / "image_sequence_attention.pt")
+
     sizes = {p.name: p.stat().st_size for p in HERE.glob("*.pt")}
     print("wrote", sizes)
 

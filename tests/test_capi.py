@@ -39,7 +39,7 @@ def test_abi_version(lib):
 def test_unsupported_dtype_is_reported_before_launch(lib):
     from powershard_b200 import _lib
     strides = _lib.i64([0, 0, 0])
-    rc = lib.ps_b200_prepass(None, None, None, strides, None, None, 0, None, 0, None, _lib.FP32,
+    rc = lib.ps_b200_prepass(None, None, None, strides, None, None, None, 0, None, 0, None, _lib.FP32,
                              1, 0, 0, 1, 1, 128, 1e-6, 1, None)
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"bf16" in lib.ps_b200_last_error()
@@ -71,12 +71,30 @@ def test_invalid_geometry(lib):
     assert b"aligned" in lib.ps_b200_last_error()
 
 
+def test_segment_row_table_is_validated(lib):
+    """The per-segment row table (image Layout balanced split) must hold
+    `world` entries within [0, seg_rows] summing to total; it is checked on
+    the host before anything touches the device."""
+    from powershard_b200 import _lib
+    ok = _lib.i32([3, 3, 2])  # split_sizes(8, 3)
+    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 3, 3, 8, ok, 2, 0, 128, 0.1,
+                                        None, None) == _lib.OK  # no valid heads: nothing to launch
+    for bad, total in (([3, 3, 3], 8), ([4, 2, 2], 8), ([3, -1, 6], 8)):
+        rc = lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 3, 3, total, _lib.i32(bad), 2, 2, 128,
+                                          0.1, None, None)
+        assert rc == _lib.ERR_INVALID, bad
+    rc = lib.ps_b200_ulysses_joint_attn_fwd(16, 16, 16, 16, _lib.BF16, _lib.BF16, 3, 3, 8, 4, _lib.i32([4, 2, 2]),
+                                            2, 2, 128, 0.1, None, None)
+    assert rc == _lib.ERR_INVALID
+    assert b"segment" in lib.ps_b200_last_error()
+
+
 def test_empty_work_is_a_no_op(lib):
     from powershard_b200 import _lib
     st = _lib.i64([0, 0, 128, 128])
     assert lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
                                 4, 1, 0, 4, 1, 4, 0.1, None, None) == _lib.OK
-    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 2, 3, 0, 2, 2, 128, 0.1, None, None) == _lib.OK
+    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 2, 3, 0, None, 2, 2, 128, 0.1, None, None) == _lib.OK
 
 
 def test_error_mapping_to_reference_exceptions():

@@ -73,6 +73,88 @@ class OracleKernels:
         out.copy_(oracle.unpack_out(out_recv, geo.total, geo.heads, geo.rank, geo.world).to(out.dtype))
 
 
+class LayoutKernels(OracleKernels):
+    """Stand-ins driven by the geometry alone (any token split, including the
+    image Layout's balanced one), for the pack-only and joint paths."""
+
+    @staticmethod
+    def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+        assert not norm_rope, "layout stand-in packs pre-normalised inputs only"
+        n, h, d = geo.n_local, geo.heads_per_rank, geo.head_dim
+        send.zero_()
+        for kind, x in enumerate((x_q, x_k, x_v)):
+            x = x.reshape(n, geo.heads, d)
+            for g in range(geo.heads):
+                send[g // h, kind, :n, g % h] = x[:, g]
+
+    @staticmethod
+    def ulysses_joint_attention(recv, prefix_qkv, out_send, prefix_out, geo, scale, status):
+        from oracle import ulysses_oracle as oracle
+        valid = geo.seg_valid()
+        hv, plen = geo.heads_valid, prefix_qkv.shape[1]
+        q, k, v = (torch.cat([prefix_qkv[kind]] + [recv[s, kind, :valid[s]] for s in range(geo.world)])
+                   for kind in range(3))
+        o = oracle.sdpa_fp32(q[None, :, :hv], k[None, :, :hv], v[None, :, :hv], scale)[0]
+        prefix_out[:, :hv] = o[:plen].to(prefix_out.dtype)
+        row = plen
+        for s in range(geo.world):
+            out_send[s, :valid[s], :hv] = o[row:row + valid[s]].to(out_send.dtype)
+            row += valid[s]
+
+    @staticmethod
+    def unpack(out_recv, out, geo):
+        h = geo.heads_per_rank
+        for g in range(geo.heads):
+            out[:, g] = out_recv[g // h, :geo.n_local, g % h].to(out.dtype)
+
+
+def image_layout_worker(rank, world, store, report, prefix, image, heads, batch, skip):
+    oracle = _setup_paths()
+    from powershard_b200.image import SequenceAttention
+    from powershard_b200.partition import ImageLayout
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        segments = [(prefix, False), (image, True)]
+        total = prefix + image
+        g = torch.Generator().manual_seed(3)
+        q, k, v = (torch.randn(batch, total, heads, 128, generator=g).bfloat16() for _ in range(3))
+        lay = ImageLayout(segments, world, rank)
+        rows = [i for s, e in oracle.image_local_ranges(segments, world, rank) for i in range(s, e)]
+        local = [t[:, rows] for t in (q, k, v)]  # [B, n, H, D]
+        if skip:
+            local = [t.transpose(1, 2).contiguous() for t in local]  # [B, H, n, D]
+        else:
+            local = [t.reshape(batch, len(rows), heads * 128) for t in local]
+        stats = {}
+        override = SequenceAttention(lay, stats, UlyssesAttention(kernels=LayoutKernels))
+        called = []
+        out = override(lambda *a, **kw: called.append(1), *local, heads, skip_reshape=skip)
+        assert not called and stats["attention_calls"] == 1
+        expected = oracle.image_sequence_attention(q.float(), k.float(), v.float(), segments, world)[rank]
+        assert out.dtype == torch.bfloat16
+        torch.testing.assert_close(out.float(), expected.reshape(batch, len(rows), heads * 128), atol=8e-3,
+                                   rtol=8e-3)  # one bf16 rounding of the output
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS", sizes=lay.sizes)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,prefix,image,heads,batch,skip",
+                         [(2, 5, 13, 3, 1, True), (3, 4, 13, 5, 2, False), (4, 0, 10, 4, 1, True)])
+def test_image_sequence_attention_over_gloo(world, prefix, image, heads, batch, skip, tmp_path, gloo_available):
+    """The Flux attention override (text replicated, image split by the
+    Layout's balanced sizes) over real gloo collectives: one all-to-all each
+    way for image rows, an all-gather over heads for text rows."""
+    report = tmp_path / "report.json"
+    mp.spawn(image_layout_worker, args=(world, str(tmp_path / "store"), str(report), prefix, image, heads, batch,
+                                        skip), nprocs=world, join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
+
+
 def _inputs(total, heads, oracle):
     g = torch.Generator().manual_seed(7)
     x = [torch.randn(1, total, heads * 128, generator=g) for _ in range(3)]

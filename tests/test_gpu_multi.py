@@ -71,3 +71,51 @@ def test_engine_over_nccl(world, total, heads, tmp_path, cuda_lib):
     for rank in range(world):
         data = json.loads(Path(f"{report}.{rank}").read_text())
         assert data["ok"], data
+
+
+def image_worker(rank, world, port, report, prefix, image, heads):
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import ulysses_oracle as oracle
+    from powershard_b200.image import SequenceAttention
+    from powershard_b200.partition import ImageLayout
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        segments = [(prefix, False), (image, True)]
+        g = torch.Generator().manual_seed(4)
+        full = [torch.randn(1, prefix + image, heads, 128, generator=g).bfloat16() for _ in range(3)]
+        rows = [i for s, e in oracle.image_local_ranges(segments, world, rank) for i in range(s, e)]
+        local = [t[:, rows].transpose(1, 2).contiguous().to(dev) for t in full]  # [1, H, n, D]
+        stats = {}
+        override = SequenceAttention(ImageLayout(segments, world, rank), stats)
+        outs = [override(None, *local, heads, skip_reshape=True) for _ in range(2)]
+        override.engine.check()
+        expected = oracle.image_sequence_attention(*(t.float() for t in full), segments, world)[rank]
+        expected = expected.reshape(1, len(rows), heads * 128)
+        errs = []
+        for out in outs:
+            err = (out.float().cpu() - expected).abs()
+            errs.append((float(err.max()), float(err.mean() / expected.abs().mean())))
+        ok = all(e <= 2e-2 and r <= 5e-3 for e, r in errs) and stats["attention_calls"] == 2
+        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,prefix,image,heads", [(2, 512, 4096, 24), (4, 77, 1001, 24), (8, 512, 4096, 24)])
+def test_image_override_over_nccl(world, prefix, image, heads, tmp_path, cuda_lib):
+    """Flux attention override (configs[4] shape, and a balanced split with
+    short middle segments) over NCCL, rank by rank against the oracle."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"NOT_RUN: needs {world} GPUs, box has {torch.cuda.device_count()}")
+    report = tmp_path / "r"
+    mp.spawn(image_worker, args=(world, _free_port(), str(report), prefix, image, heads), nprocs=world, join=True)
+    for rank in range(world):
+        data = json.loads(Path(f"{report}.{rank}").read_text())
+        assert data["ok"], data

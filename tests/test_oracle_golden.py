@@ -131,3 +131,37 @@ def test_product_rope_tables_match_oracle(oracle):
     for grid in ((2, 3, 4), (21, 30, 52)):
         torch.testing.assert_close(rope.rope_table_3d(grid, 128), oracle.rope_table_3d(grid, 128)[0, :, 0])
     torch.testing.assert_close(rope.rope_table_flux(5, (4, 6), 128), oracle.rope_table_flux(5, (4, 6), 128)[0, :, 0])
+
+
+@pytest.mark.parametrize("index", range(4))
+def test_image_sequence_attention_matches_reference(oracle, golden_dir, index):
+    """image_parallel.SequenceAttention over image_layout.Layout (balanced
+    split of the image segment, replicated text/reference segments)."""
+    case = load(golden_dir, "image_sequence_attention.pt")[index]
+    world, heads = case["world"], case["heads"]
+    q, k, v = (t.transpose(1, 2) for t in (case["q"], case["k"], case["v"]))  # BHLD -> BLHD
+    split = [n for n, s in case["segments"] if s][0]
+    outs = oracle.image_sequence_attention(q, k, v, case["segments"], world)
+    for r, ref in enumerate(case["ranks"]):
+        assert oracle.split_sizes(split, world) == ref["sizes"]
+        assert oracle.image_local_ranges(case["segments"], world, r) == [tuple(x) for x in ref["local_ranges"]]
+        got = outs[r].reshape(outs[r].shape[0], outs[r].shape[1], -1)
+        assert got.shape[1] == ref["local_len"]
+        torch.testing.assert_close(got, ref["out"], atol=1e-6, rtol=1e-5)
+        assert ref["stats"]["attention_calls"] == 1
+
+
+def test_product_image_layout_matches_oracle(oracle, golden_dir):
+    """powershard_b200.partition.ImageLayout / split_sizes and a geometry
+    built from the layout agree with the recorded reference Layout."""
+    from powershard_b200.partition import ImageLayout, UlyssesGeometry, split_sizes
+    for case in load(golden_dir, "image_sequence_attention.pt"):
+        world = case["world"]
+        split = [n for n, s in case["segments"] if s][0]
+        for r, ref in enumerate(case["ranks"]):
+            lay = ImageLayout(case["segments"], world, r)
+            assert lay.sizes == ref["sizes"] == split_sizes(split, world)
+            assert (lay.local_len, lay.chunk) == (ref["local_len"], ref["chunk"])
+            geo = UlyssesGeometry(total=split, heads=5, head_dim=128, world=world, rank=r, sizes=lay.sizes)
+            assert geo.width == lay.chunk and geo.seg_valid() == lay.sizes
+            assert geo.bounds == (lay.a - lay.split_start, lay.b - lay.split_start)
