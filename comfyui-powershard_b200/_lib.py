@@ -22,6 +22,7 @@ BF16, FP16, FP32 = 0, 1, 2
 # Every symbol of include/ps_b200.h with its ctypes signature.
 _c_i64p = ctypes.POINTER(ctypes.c_int64)
 _c_intp = ctypes.c_void_p
+_c_ptrs = ctypes.POINTER(ctypes.c_void_p)  # void* const* (one pointer per rank)
 SIGNATURES = {
     "ps_b200_abi_version": (ctypes.c_int, []),
     "ps_b200_last_error": (ctypes.c_char_p, []),
@@ -52,7 +53,25 @@ SIGNATURES = {
     "ps_b200_unpack": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "ps_b200_unpack_strided": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "ps_b200_prepass_to": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, _c_i64p,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64,
+        _c_ptrs, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+    "ps_b200_ulysses_attn_to": (ctypes.c_int, [
+        ctypes.c_void_p, _c_ptrs, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+        _c_intp, ctypes.c_void_p]),
+    "ps_b200_shared_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "ps_b200_shared_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "ps_b200_ipc_export": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte)]),
+    "ps_b200_ipc_import": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_void_p)]),
+    "ps_b200_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
 }
+IPC_HANDLE_BYTES = 64
 
 _LIB = None
 
@@ -118,6 +137,12 @@ def i32(values):
         return None
     values = [int(v) for v in values]
     return (ctypes.c_int * len(values))(*values)
+
+
+def ptrs(values):
+    """ctypes void* array of device addresses (one per rank)."""
+    values = [int(v) for v in values]
+    return (ctypes.c_void_p * len(values))(*values)
 
 
 def i64(values):

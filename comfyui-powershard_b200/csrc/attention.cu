@@ -455,40 +455,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) ok = warp_wait(bar(kBarO), 0, abort_flag, status, kErrO);
     tc_fence_after();
-    if (ok) {
-      const int tq = t ? tq1 : tq0;
-      bool pre = false;
-      int seg = 0, row0 = 0, valid = 0;
-      if (tq < args.num_q_tiles) q_tile(args, tq, pre, seg, row0, valid);
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      const bool store = row < valid;
-      void* const obase = pre ? args.pre_out : args.out;
-      const int64_t* ost = pre ? args.pre_o_stride : args.o_stride;
-      const int64_t oidx = batch * ost[0] + seg * ost[1] + static_cast<int64_t>(row0 + row) * ost[2] +
-                           head * ost[3];
+    const int tq = t ? tq1 : tq0;
+    bool pre = false;
+    int seg = 0, row0 = 0, valid = 0;
+    if (tq < args.num_q_tiles) q_tile(args, tq, pre, seg, row0, valid);
+    const float inv_l = l > 0.f ? 1.f / l : 0.f;
+    void* const obase = pre ? args.pre_out : args.seg_out[seg];
+    const int64_t* ost = pre ? args.pre_o_stride : args.o_stride;
+    const int64_t otile = batch * ost[0] + static_cast<int64_t>(row0) * ost[2] + head * ost[3];
+    if (args.out_fp32) {
+      // tcgen05.ld is warp-collective: every lane loads, only valid rows store.
+      if (ok) {
+        float* orow = reinterpret_cast<float*>(obase) + otile + static_cast<int64_t>(row) * ost[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + 32 * c, o);
-        tmem_wait_ld();
-        if (store) {
-          if (args.out_fp32) {
-            float4* orow = reinterpret_cast<float4*>(reinterpret_cast<float*>(obase) + oidx + 32 * c);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+          if (row < valid) {
+            float4* dst = reinterpret_cast<float4*>(orow + 32 * c);
 #pragma unroll
             for (int u = 0; u < 8; ++u)
-              orow[u] = make_float4(__uint_as_float(o[4 * u + 0]) * inv_l, __uint_as_float(o[4 * u + 1]) * inv_l,
-                                    __uint_as_float(o[4 * u + 2]) * inv_l, __uint_as_float(o[4 * u + 3]) * inv_l);
-          } else {
-            uint16_t* orow = reinterpret_cast<uint16_t*>(obase) + oidx + 32 * c;
+              dst[u] = make_float4(__uint_as_float(o[4 * u + 0]) * inv_l, __uint_as_float(o[4 * u + 1]) * inv_l,
+                                   __uint_as_float(o[4 * u + 2]) * inv_l, __uint_as_float(o[4 * u + 3]) * inv_l);
+          }
+        }
+      }
+    } else {
+      // Stage the 16-bit tile in K stage t (idle once every UMMA has
+      // completed): row r, 16-byte chunk k at r*256 + ((k ^ (r & 15)) << 4),
+      // so both the row-per-thread writes and the row-major reads below touch
+      // each bank group once per 128 bytes.  Then 16 threads store each
+      // 256-byte output row with consecutive 16-byte stores, which keeps the
+      // rows whole when they cross NVLink.
+      uint8_t* stage = sK + t * kTileBytes;
+      if (ok) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 v;
-              v.x = pack2<kFp16>(__uint_as_float(o[8 * u + 0]) * inv_l, __uint_as_float(o[8 * u + 1]) * inv_l);
-              v.y = pack2<kFp16>(__uint_as_float(o[8 * u + 2]) * inv_l, __uint_as_float(o[8 * u + 3]) * inv_l);
-              v.z = pack2<kFp16>(__uint_as_float(o[8 * u + 4]) * inv_l, __uint_as_float(o[8 * u + 5]) * inv_l);
-              v.w = pack2<kFp16>(__uint_as_float(o[8 * u + 6]) * inv_l, __uint_as_float(o[8 * u + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(orow + 8 * u) = v;
-            }
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 v;
+            v.x = pack2<kFp16>(__uint_as_float(o[8 * u + 0]) * inv_l, __uint_as_float(o[8 * u + 1]) * inv_l);
+            v.y = pack2<kFp16>(__uint_as_float(o[8 * u + 2]) * inv_l, __uint_as_float(o[8 * u + 3]) * inv_l);
+            v.z = pack2<kFp16>(__uint_as_float(o[8 * u + 4]) * inv_l, __uint_as_float(o[8 * u + 5]) * inv_l);
+            v.w = pack2<kFp16>(__uint_as_float(o[8 * u + 6]) * inv_l, __uint_as_float(o[8 * u + 7]) * inv_l);
+            const int k = 4 * c + u;
+            *reinterpret_cast<uint4*>(stage + row * 256 + ((k ^ (row & 15)) << 4)) = v;
+          }
+        }
+      }
+      named_bar_sync(1 + t, 128);  // all 128 threads of the group, whatever their wait outcome
+      if (ok) {
+        const int sub = threadIdx.x & 127;
+        const int k = sub & 15;
+        uint16_t* const obase16 = reinterpret_cast<uint16_t*>(obase) + otile + 8 * k;
+#pragma unroll 4
+        for (int p = 0; p < 16; ++p) {
+          const int r = p * 8 + (sub >> 4);
+          if (r < valid) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 256 + ((k ^ (r & 15)) << 4));
+            *reinterpret_cast<uint4*>(obase16 + static_cast<int64_t>(r) * ost[2]) = v;
           }
         }
       }

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 namespace psb {
@@ -125,7 +126,7 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
                      int head_dim,
                      int seg_rows_q, int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k,
                      float softmax_scale, int* status, void* stream, const Prefix* pre = nullptr,
-                     const int* seg_valid = nullptr) {
+                     const int* seg_valid = nullptr, void* const* seg_out = nullptr) {
   const int pre_len = pre ? pre->len : 0;
   if (segs_q > kMaxSegs || segs_k > kMaxSegs)
     return set_error(PS_B200_ERR_UNSUPPORTED, "more than %d segments", kMaxSegs);
@@ -144,9 +145,13 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
     return set_error(PS_B200_ERR_INVALID, "len exceeds segments * seg_rows");
   if (batch > 65535 || grid_heads > 65535) return set_error(PS_B200_ERR_UNSUPPORTED, "batch/heads above 65535");
   if (!std::isfinite(softmax_scale)) return set_error(PS_B200_ERR_INVALID, "softmax_scale must be finite");
-  if (!q.ptr || !k.ptr || !v.ptr || !out) return set_error(PS_B200_ERR_INVALID, "null tensor pointer");
+  if (!q.ptr || !k.ptr || !v.ptr || (!out && !seg_out)) return set_error(PS_B200_ERR_INVALID, "null tensor pointer");
   if (!aligned16(q.ptr) || !aligned16(k.ptr) || !aligned16(v.ptr) || !aligned16(out))
     return set_error(PS_B200_ERR_INVALID, "tensor pointers must be 16-byte aligned");
+  if (seg_out)
+    for (int s = 0; s < segs_q; ++s)
+      if (!seg_out[s] || !aligned16(seg_out[s]))
+        return set_error(PS_B200_ERR_INVALID, "segment %d output pointer null or not 16-byte aligned", s);
   if (pre_len) {
     if (!pre->q.ptr || !pre->k.ptr || !pre->v.ptr || !pre->out)
       return set_error(PS_B200_ERR_INVALID, "null prefix tensor pointer");
@@ -174,7 +179,9 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
     if (int rc = make_map(&tvp, pre->v.ptr, fp16, head_dim, pre->v.heads, pre_len, 1, batch, pre->v.st)) return rc;
   }
   AttnArgs a{};
-  a.out = out;
+  const int64_t osize = out_dtype == PS_B200_FP32 ? 4 : 2;
+  for (int s = 0; s < segs_q; ++s)
+    a.seg_out[s] = seg_out ? seg_out[s] : static_cast<void*>(static_cast<char*>(out) + s * out_st[1] * osize);
   for (int i = 0; i < 4; ++i) a.o_stride[i] = out_st[i];
   a.seg_rows_q = seg_rows_q;
   a.nsegs_q = segs_q;
@@ -229,16 +236,13 @@ int set_cuda_error(const char* what, cudaError_t err) {
 
 using namespace psb;
 
-extern "C" {
-
-int ps_b200_abi_version(void) { return PS_B200_ABI_VERSION; }
-
-const char* ps_b200_last_error(void) { return psb::g_msg; }
-
-int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
-                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
-                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
-                    int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream) {
+// Shared body of ps_b200_prepass / ps_b200_prepass_to: dst[d] is the
+// [3][seg_rows][heads_per_rank][head_dim] block for destination rank d.
+static int prepass_common(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                   const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                   const float* freqs, int64_t freqs_row_stride, void* const* dst, int dtype,
+                   int world, int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
+                   int norm_rope, void* stream) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
   if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
       int64_t(heads_per_rank) * world < heads || head_dim <= 0)
@@ -250,7 +254,6 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   if (int64_t(heads) * head_dim > 8192)
     return set_error(PS_B200_ERR_UNSUPPORTED, "heads*head_dim above 8192 is not supported");
   if (seg_rows == 0) return PS_B200_OK;
-  if (!send || !aligned16(send)) return set_error(PS_B200_ERR_INVALID, "send buffer null or not 16-byte aligned");
   if (n_local > 0) {
     const void* xs[3] = {x_q, x_k, x_v};
     for (int i = 0; i < 3; ++i)
@@ -282,7 +285,7 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   a.w_fp32 = w_dtype == PS_B200_FP32;
   a.freqs = freqs;
   a.freqs_row_stride = freqs_row_stride;
-  a.send = send;
+  for (int d = 0; d < world; ++d) a.dst[d] = dst[d];
   a.world = world;
   a.n_local = n_local;
   a.seg_rows = seg_rows;
@@ -292,6 +295,47 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   a.eps = eps;
   a.norm_rope = norm_rope;
   return launch_prepass(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
+}
+
+
+extern "C" {
+
+int ps_b200_abi_version(void) { return PS_B200_ABI_VERSION; }
+
+const char* ps_b200_last_error(void) { return psb::g_msg; }
+
+int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local,
+                    int seg_rows, int heads, int heads_per_rank, int head_dim, float eps, int norm_rope,
+                    void* stream) {
+  if (world < 1 || world > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "world must be in [1, %d]", kMaxSegs);
+  if (!send || !aligned16(send)) {
+    if (seg_rows > 0) return set_error(PS_B200_ERR_INVALID, "send buffer null or not 16-byte aligned");
+  }
+  void* dst[kMaxSegs];
+  const int64_t block = int64_t(3) * seg_rows * heads_per_rank * head_dim * 2;  // bytes of one destination block
+  for (int d = 0; d < world; ++d) dst[d] = static_cast<char*>(send) + d * block;
+  return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
+                        freqs_row_stride, dst, dtype, world, n_local, seg_rows, heads, heads_per_rank, head_dim,
+                        eps, norm_rope, stream);
+}
+
+int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                       const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                       const float* freqs, int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int world,
+                       int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
+                       int norm_rope, void* stream) {
+  if (world < 1 || world > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "world must be in [1, %d]", kMaxSegs);
+  if (seg_rows > 0) {
+    if (!dst_blocks) return set_error(PS_B200_ERR_INVALID, "null destination table");
+    for (int d = 0; d < world; ++d)
+      if (!dst_blocks[d] || !aligned16(dst_blocks[d]))
+        return set_error(PS_B200_ERR_INVALID, "destination block %d null or not 16-byte aligned", d);
+  }
+  return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
+                        freqs_row_stride, dst_blocks, dtype, world, n_local, seg_rows, heads, heads_per_rank,
+                        head_dim, eps, norm_rope, stream);
 }
 
 int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
@@ -327,6 +371,31 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
   SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows, world, total,
                           seg_rows, world, total, softmax_scale, status, stream, nullptr, seg_valid);
+}
+
+int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t out_row_stride, int dtype,
+                            int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
+                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, int* status,
+                            void* stream) {
+  if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
+      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
+  if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
+  if (total == 0 || heads_valid == 0) return PS_B200_OK;
+  if (!out_blocks) return set_error(PS_B200_ERR_INVALID, "null output table");
+  if (out_row_stride < int64_t(heads_valid) * head_dim)
+    return set_error(PS_B200_ERR_INVALID, "output row stride below heads_valid * head_dim");
+  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows;
+  const int64_t block = n * h * D;
+  const char* base = static_cast<const char*>(recv);
+  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
+  const int64_t out_st[4] = {0, 0, out_row_stride, D};
+  SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  return attention_common(tq, tk, tv, nullptr, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
+                          world, total, seg_rows, world, total, softmax_scale, status, stream, nullptr, seg_valid,
+                          out_blocks);
 }
 
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
@@ -367,30 +436,94 @@ int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, voi
 
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
                    int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream) {
+  if (world < 1 || n_local > seg_rows || heads_per_rank < 1 || int64_t(heads_per_rank) * world < heads)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent unpack geometry");
+  return ps_b200_unpack_strided(recv, int64_t(seg_rows) * heads_per_rank * head_dim,
+                                int64_t(heads_per_rank) * head_dim, out, out_row_stride, dtype, out_dtype, n_local,
+                                heads, heads_per_rank, head_dim, stream);
+}
+
+int ps_b200_unpack_strided(const void* recv, int64_t src_stride, int64_t row_stride, void* out,
+                           int64_t out_row_stride, int dtype, int out_dtype, int n_local, int heads,
+                           int heads_per_rank, int head_dim, void* stream) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "unpack supports bf16 and fp16 inputs only");
   if (out_dtype != dtype && out_dtype != PS_B200_FP32)
     return set_error(PS_B200_ERR_UNSUPPORTED, "unpack output must be fp32 or the input dtype");
-  if (world < 1 || n_local < 0 || n_local > seg_rows || heads < 1 || heads_per_rank < 1 ||
-      int64_t(heads_per_rank) * world < heads || head_dim <= 0 || head_dim % 8 != 0)
+  if (n_local < 0 || heads < 1 || heads_per_rank < 1 || head_dim <= 0 || head_dim % 8 != 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent unpack geometry");
   if (int64_t(n_local) * heads * (head_dim / 8) >= (int64_t(1) << 31))
     return set_error(PS_B200_ERR_UNSUPPORTED, "unpack size above 2^31 vectors");
   if (n_local == 0) return PS_B200_OK;
-  if (!recv || !out || !aligned16(recv) || !aligned16(out) || out_row_stride % 8 != 0 || out_row_stride < 0)
-    return set_error(PS_B200_ERR_INVALID, "unpack buffers must be 16-byte aligned, row stride %% 8 == 0");
+  if (!recv || !out || !aligned16(recv) || !aligned16(out) || out_row_stride % 8 != 0 || out_row_stride < 0 ||
+      src_stride % 8 != 0 || src_stride < 0 || row_stride % 8 != 0 || row_stride < 0)
+    return set_error(PS_B200_ERR_INVALID, "unpack buffers must be 16-byte aligned, strides %% 8 == 0");
   if (int rc = check_device()) return rc;
   UnpackArgs a{};
   a.recv = recv;
+  a.src_stride = src_stride;
+  a.row_stride = row_stride;
   a.out = out;
   a.out_row_stride = out_row_stride;
-  a.world = world;
+  a.world = (heads + heads_per_rank - 1) / heads_per_rank;
   a.n_local = n_local;
-  a.seg_rows = seg_rows;
+  a.seg_rows = n_local;
   a.heads = heads;
   a.heads_per_rank = heads_per_rank;
   a.head_dim = head_dim;
   a.out_fp32 = out_dtype == PS_B200_FP32;
   return launch_unpack(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- shared buffers
+int ps_b200_shared_alloc(size_t bytes, void** ptr) {
+  if (!ptr) return set_error(PS_B200_ERR_INVALID, "null output pointer");
+  *ptr = nullptr;
+  if (bytes == 0) return set_error(PS_B200_ERR_INVALID, "zero-byte shared buffer");
+  if (int rc = check_device()) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return set_cuda_error("cudaMalloc (shared buffer)", e);
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_cuda_error("cudaMemset (shared buffer)", e);
+  }
+  *ptr = p;
+  return PS_B200_OK;
+}
+
+int ps_b200_shared_free(void* ptr) {
+  if (!ptr) return PS_B200_OK;
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? PS_B200_OK : set_cuda_error("cudaFree (shared buffer)", e);
+}
+
+int ps_b200_ipc_export(const void* ptr, unsigned char* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == PS_B200_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle) return set_error(PS_B200_ERR_INVALID, "null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return set_cuda_error("cudaIpcGetMemHandle", e);
+  std::memcpy(handle, &h, sizeof(h));
+  return PS_B200_OK;
+}
+
+int ps_b200_ipc_import(const unsigned char* handle, void** ptr) {
+  if (!ptr || !handle) return set_error(PS_B200_ERR_INVALID, "null pointer");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_cuda_error("cudaIpcOpenMemHandle", e);
+  *ptr = p;
+  return PS_B200_OK;
+}
+
+int ps_b200_ipc_close(void* ptr) {
+  if (!ptr) return PS_B200_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? PS_B200_OK : set_cuda_error("cudaIpcCloseMemHandle", e);
 }
 
 }  // extern "C"

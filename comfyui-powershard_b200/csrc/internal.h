@@ -11,8 +11,9 @@ constexpr int kMaxSegs = 64;  // segments (source ranks) per attention call
 
 // Arguments of the attention kernel that are not tensor maps.
 struct AttnArgs {
-  void* out;             // output element (batch 0, seg 0, row 0, head 0, d 0)
-  int64_t o_stride[4];   // batch, segment, row, head strides in elements (d stride 1)
+  void* seg_out[kMaxSegs];  // output element (batch 0, row 0, head 0, d 0) of each query segment:
+                            // slices of one tensor, or other GPUs' buffers (peer exchange)
+  int64_t o_stride[4];   // batch, (unused), row, head strides in elements (d stride 1)
   int seg_rows_q;        // rows allocated per query segment
   int nsegs_q;           // query segments
   int q_tiles_per_seg;   // ceil(seg_rows_q / 128)
@@ -47,7 +48,8 @@ struct PrepassArgs {
   int w_fp32;              // 1: weights are fp32, 0: same 16-bit type as x
   const float* freqs;      // [n_local][head_dim/2][2][2] fp32
   int64_t freqs_row_stride;// floats between consecutive tokens
-  void* send;              // [world][3][seg_rows][heads_per_rank][head_dim]
+  void* dst[kMaxSegs];     // block [3][seg_rows][heads_per_rank][head_dim] for each destination rank:
+                           // slices of the local send buffer, or peers' receive buffers
   int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
   float eps;
   int norm_rope;           // 0: plain pack, 1: full-width RMSNorm + RoPE, 2: per-head RMSNorm + RoPE
@@ -56,7 +58,8 @@ struct PrepassArgs {
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);
 
 struct UnpackArgs {
-  const void* recv;        // [world][seg_rows][heads_per_rank][head_dim]
+  const void* recv;        // head block src, row i at recv + src*src_stride + i*row_stride (elements)
+  int64_t src_stride, row_stride;
   void* out;               // [n_local][heads][head_dim] (row stride below)
   int64_t out_row_stride;  // elements between consecutive tokens of out
   int world, n_local, seg_rows, heads, heads_per_rank, head_dim;

@@ -84,13 +84,12 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
   const int h = a.heads_per_rank;
   const int vph = D >> 3;             // vectors per head
   const int nvec = a.heads * vph;     // vectors per token row
-  uint16_t* send = static_cast<uint16_t*>(a.send);
   const int64_t block_elems = static_cast<int64_t>(a.seg_rows) * h * D;  // one [seg_rows][h][D] block
-  auto slot = [&](int kind, int g, int dd) -> int64_t {
+  auto slot = [&](int kind, int g, int dd) -> uint4* {
     const int dst = g / h;
     const int j = g - dst * h;
-    return (static_cast<int64_t>(dst) * 3 + kind) * block_elems + static_cast<int64_t>(i) * h * D +
-           static_cast<int64_t>(j) * D + dd;
+    return reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.dst[dst]) + kind * block_elems +
+                                    static_cast<int64_t>(i) * h * D + static_cast<int64_t>(j) * D + dd);
   };
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
 
@@ -99,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
     for (int kind = 0; kind < 3; ++kind)
       for (int v = tid; v < total; v += kThreads) {
         const int g = v / vph;
-        *reinterpret_cast<uint4*>(send + slot(kind, g, (v - g * vph) * 8)) = zero;
+        *slot(kind, g, (v - g * vph) * 8) = zero;
       }
     return;
   }
@@ -189,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
         }
         outv = pack8(o);
       }
-      *reinterpret_cast<uint4*>(send + slot(kind, g, dd)) = outv;
+      *slot(kind, g, dd) = outv;
     }
   }
   // Head padding: slots of heads [heads, world*h) are zero.
@@ -197,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
   for (int kind = 0; kind < 3; ++kind)
     for (int v = tid; v < padded; v += kThreads) {
       const int g = a.heads + v / vph;
-      *reinterpret_cast<uint4*>(send + slot(kind, g, (v % vph) * 8)) = zero;
+      *slot(kind, g, (v % vph) * 8) = zero;
     }
 }
 
@@ -217,8 +216,8 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
     const int dd = (rem - g * vph) * 8;
     const int src = g / h;
     const int j = g - src * h;
-    const uint16_t* in = static_cast<const uint16_t*>(a.recv) +
-                         ((static_cast<int64_t>(src) * a.seg_rows + i) * h + j) * D + dd;
+    const uint16_t* in = static_cast<const uint16_t*>(a.recv) + src * a.src_stride + i * a.row_stride +
+                         static_cast<int64_t>(j) * D + dd;
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(in));
     const int64_t o = static_cast<int64_t>(i) * a.out_row_stride + static_cast<int64_t>(g) * D + dd;
     if constexpr (kOutFp32) {

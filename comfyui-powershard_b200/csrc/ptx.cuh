@@ -34,6 +34,12 @@ __device__ __forceinline__ uint32_t lane_id() {
   return l;
 }
 
+// Barrier over `count` threads (a multiple of 32) of the CTA on hardware
+// barrier `id` (1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

@@ -60,19 +60,9 @@ def _check16(t: torch.Tensor, what: str):
 NORM_NONE, NORM_FULL, NORM_PER_HEAD = 0, 1, 2
 
 
-def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: float = 1e-6,
-            norm_rope=True):
-    """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
-
-    x_*: [n_local, H*D] (row stride may exceed H*D) or [n_local, H, D] with
-    any row and head strides (e.g. a [H, L, D] tensor transposed) and unit
-    inner stride; freqs: [n_local, D/2, 2, 2] fp32.  norm_rope: False/0 pack
-    only, True/1 RMSNorm over the full width (Wan; w_* [H*D]), 2 RMSNorm per
-    head (Flux QK-norm; w_* [D]).
-    """
-    mode = int(norm_rope)
-    lib = _lib.load()
-    for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v"), (send, "send")):
+def _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo: UlyssesGeometry, dtype, device, mode: int):
+    """Validated pointer / stride arguments shared by the two pre-pass entry points."""
+    for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v")):
         _check16(t, f"prepass {name}")
     n = geo.n_local
     width = geo.heads * geo.head_dim
@@ -85,35 +75,68 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
         else:
             raise ValueError(f"prepass {name}: expected [{n}, {width}] or [{n}, {geo.heads}, {geo.head_dim}] "
                              f"with unit inner stride, got {tuple(t.shape)} / {t.stride()}")
-        if t.dtype != send.dtype:
-            raise ValueError("prepass: q/k/v and send dtypes differ")
-    if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
-        raise ValueError(f"prepass: send must be contiguous {geo.send_shape()}")
-    w_dtype = _lib.dtype_code(send.dtype)
+        if t.dtype != dtype:
+            raise ValueError("prepass: q/k/v and exchange dtypes differ")
+    w_dtype = _lib.dtype_code(dtype)
     fptr, fstride = 0, 0
     wq = wk = 0
     if mode:
         wlen = width if mode == NORM_FULL else geo.head_dim
         for t, name in ((w_q, "w_q"), (w_k, "w_k")):
-            if t.dim() != 1 or t.shape[0] != wlen or not t.is_contiguous() or t.device != send.device:
-                raise ValueError(f"prepass {name}: expected contiguous [{wlen}] on {send.device}")
+            if t.dim() != 1 or t.shape[0] != wlen or not t.is_contiguous() or t.device != device:
+                raise ValueError(f"prepass {name}: expected contiguous [{wlen}] on {device}")
         if w_q.dtype != w_k.dtype:
             raise ValueError("prepass: norm weights must share a dtype")
         w_dtype = _lib.dtype_code(w_q.dtype)
         wq, wk = w_q.data_ptr(), w_k.data_ptr()
-        if freqs.dtype != torch.float32 or freqs.device != send.device:
-            raise ValueError("prepass: freqs must be fp32 on the send device")
+        if freqs.dtype != torch.float32 or freqs.device != device:
+            raise ValueError("prepass: freqs must be fp32 on the exchange device")
         if (freqs.dim() != 4 or freqs.shape[0] != n or tuple(freqs.shape[1:]) != (geo.head_dim // 2, 2, 2)
                 or freqs.stride()[1:] != (4, 2, 1) or freqs.stride(0) % 4 != 0):
             raise ValueError(f"prepass: freqs must be [{n}, {geo.head_dim // 2}, 2, 2] with contiguous rows")
         fptr, fstride = freqs.data_ptr(), freqs.stride(0)
+    return [x_q.data_ptr(), x_k.data_ptr(), x_v.data_ptr(),
+            _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]), _lib.i64(head_strides),
+            wq, wk, w_dtype, fptr, fstride]
+
+
+def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: float = 1e-6,
+            norm_rope=True):
+    """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
+
+    x_*: [n_local, H*D] (row stride may exceed H*D) or [n_local, H, D] with
+    any row and head strides (e.g. a [H, L, D] tensor transposed) and unit
+    inner stride; freqs: [n_local, D/2, 2, 2] fp32.  norm_rope: False/0 pack
+    only, True/1 RMSNorm over the full width (Wan; w_* [H*D]), 2 RMSNorm per
+    head (Flux QK-norm; w_* [D]).
+    """
+    mode = int(norm_rope)
+    lib = _lib.load()
+    _check16(send, "prepass send")
+    if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
+        raise ValueError(f"prepass: send must be contiguous {geo.send_shape()}")
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, send.dtype, send.device, mode)
     rc = lib.ps_b200_prepass(
-        x_q.data_ptr(), x_k.data_ptr(), x_v.data_ptr(),
-        _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]), _lib.i64(head_strides),
-        wq, wk, w_dtype, fptr, fstride, send.data_ptr(), _lib.dtype_code(send.dtype),
-        geo.world, n, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
+        *args, send.data_ptr(), _lib.dtype_code(send.dtype),
+        geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
         mode, _lib.stream_handle(send.device))
     _lib.check(rc, "ps_b200_prepass")
+
+
+def prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, dst_blocks, geo: UlyssesGeometry, dtype: torch.dtype,
+               eps: float = 1e-6, norm_rope=True):
+    """``prepass`` storing destination d's [3,width,h,D] block at the device
+    address ``dst_blocks[d]`` (a peer's receive buffer: the fused exchange)."""
+    mode = int(norm_rope)
+    lib = _lib.load()
+    if len(dst_blocks) != geo.world:
+        raise ValueError(f"prepass_to: {len(dst_blocks)} destination blocks for {geo.world} ranks")
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, dtype, x_q.device, mode)
+    rc = lib.ps_b200_prepass_to(
+        *args, _lib.ptrs(dst_blocks), _lib.dtype_code(dtype),
+        geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
+        mode, _lib.stream_handle(x_q.device))
+    _lib.check(rc, "ps_b200_prepass_to")
 
 
 def _seg_table(geo: UlyssesGeometry):
@@ -187,6 +210,49 @@ def unpack(out_recv, out, geo: UlyssesGeometry):
         _lib.dtype_code(out.dtype), geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank,
         geo.head_dim, _lib.stream_handle(out.device))
     _lib.check(rc, "ps_b200_unpack")
+
+
+def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch.dtype, geo: UlyssesGeometry,
+                         scale: float, status: DeviceStatus | None):
+    """``ulysses_attention`` storing segment s's valid rows at the device
+    address ``out_blocks[s]`` (row stride ``out_row_stride`` elements, head j
+    at + j*D): each source rank's staging buffer, the fused output exchange."""
+    lib = _lib.load()
+    _check16(recv, "attention recv")
+    if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
+        raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")
+    if len(out_blocks) != geo.world:
+        raise ValueError(f"attention: {len(out_blocks)} output blocks for {geo.world} ranks")
+    if out_dtype not in (recv.dtype, torch.float32):
+        raise ValueError("attention: output dtype must be fp32 or the input dtype")
+    rc = lib.ps_b200_ulysses_attn_to(
+        recv.data_ptr(), _lib.ptrs(out_blocks), int(out_row_stride), _lib.dtype_code(recv.dtype),
+        _lib.dtype_code(out_dtype), geo.world, geo.width, geo.total, _seg_table(geo), geo.heads_per_rank,
+        geo.heads_valid, geo.head_dim, float(scale), status.ptr if status is not None else None,
+        _lib.stream_handle(recv.device))
+    _lib.check(rc, "ps_b200_ulysses_attn_to")
+    if status is not None:
+        status.arm()
+
+
+def unpack_staged(staging, out, geo: UlyssesGeometry):
+    """Staging buffer [width, W*h, D] (rows of this rank, every head block) ->
+    out [n_local, H, D] (real heads only)."""
+    lib = _lib.load()
+    _check16(staging, "unpack staging")
+    _lib.require_cuda(out, "unpack out")
+    shape = (geo.width, geo.padded_heads, geo.head_dim)
+    if tuple(staging.shape) != shape or not staging.is_contiguous():
+        raise ValueError(f"unpack: staging must be contiguous {shape}")
+    if (out.dim() != 3 or tuple(out.shape) != (geo.n_local, geo.heads, geo.head_dim)
+            or out.stride(2) != 1 or out.stride(1) != geo.head_dim):
+        raise ValueError(f"unpack: out must be [{geo.n_local}, {geo.heads}, {geo.head_dim}] with packed heads")
+    h, d = geo.heads_per_rank, geo.head_dim
+    rc = lib.ps_b200_unpack_strided(
+        staging.data_ptr(), h * d, geo.padded_heads * d, out.data_ptr(), out.stride(0),
+        _lib.dtype_code(staging.dtype), _lib.dtype_code(out.dtype), geo.n_local, geo.heads, h, d,
+        _lib.stream_handle(out.device))
+    _lib.check(rc, "ps_b200_unpack_strided")
 
 
 def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None):

@@ -12,6 +12,12 @@ Data path (one process per GPU, NCCL through torch.distributed):
   all_to_all_single out_send -> out_recv
   unpack kernel     out_recv -> [n][H][D], dropping padded heads
 
+With the peer exchange (one node, NVLink; ``exchange="auto"|"peer"``) the
+two all_to_all_single calls disappear: the pre-pass stores each
+destination's block straight into that rank's receive buffer, the attention
+epilogue stores each output row straight into its owner's staging buffer,
+and two 4-byte all-reduces order the steps across ranks (``peer.py``).
+
 This replaces, for one batch row, powershard/wan_model.py:421-430
 (attention_qkv) + 343-364 (ulysses_to_sequence) + 398-418 (run_attention) +
 367-381 (ulysses_to_heads).  Buffers are cached per (device, stream,
@@ -36,13 +42,24 @@ class UlyssesAttention:
     with the same buffer contracts).  Only tests replace it, to exercise the
     exchange logic over CPU collectives; CPU tensors given to the default
     kernels raise.
+
+    ``exchange`` picks how q/k/v and outputs cross ranks: ``"nccl"`` - two
+    ``all_to_all_single`` calls per block, as the reference; ``"peer"`` - the
+    kernels store straight into the other ranks' buffers over NVLink
+    (``peer.PeerExchange``; raises if the ranks cannot map each other's
+    memory); ``"auto"`` (default) - peer when the group is NCCL on one node
+    and every rank can map its peers, else nccl.
     """
 
-    def __init__(self, group=None, kernels=None):
+    def __init__(self, group=None, kernels=None, exchange: str = "auto"):
+        if exchange not in ("auto", "nccl", "peer"):
+            raise ValueError(f"exchange must be auto, nccl or peer, not {exchange!r}")
         self.group = group
         self.kernels = kernels if kernels is not None else ops
+        self.exchange = exchange
         self._buffers = {}
         self._status = {}
+        self._peers = {}
 
     # ------------------------------------------------------------ topology
     def world_rank(self):
@@ -70,13 +87,34 @@ class UlyssesAttention:
             out_recv = None if geo.world == 1 else torch.empty_like(out_send)
             ws = dict(send=send, recv=recv, out_send=out_send, out_recv=out_recv)
             self._buffers[key] = ws
-        if device.index not in self._status:
-            self._status[device.index] = self.kernels.DeviceStatus(device)
-        return ws, self._status[device.index]
+        return ws, self._device_status(device)
 
     def _exchange(self, recv, send, geo):
         if geo.world > 1:
             dist.all_to_all_single(recv, send, group=self.group)
+
+    def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
+        """The peer exchange of this geometry, or None for the NCCL path."""
+        if geo.world == 1 or self.exchange == "nccl" or self.kernels is not ops or device.type != "cuda":
+            return None
+        if self.exchange == "auto" and dist.get_backend(self.group) != "nccl":
+            return None
+        stream = torch.cuda.current_stream(device).cuda_stream
+        key = (device.index, stream, geo.world, geo.rank, geo.width, geo.heads_per_rank, geo.head_dim, dtype)
+        if key not in self._peers:
+            from .peer import PeerExchange
+            ex = PeerExchange.create(self.group, geo, dtype, device)
+            if ex is None and self.exchange == "peer":
+                raise RuntimeError("peer exchange requested but the ranks cannot map each other's memory")
+            self._peers[key] = ex
+        return self._peers[key]
+
+    def close(self):
+        """Release peer-exchange buffers (collective: call on every rank)."""
+        for ex in self._peers.values():
+            if ex is not None:
+                ex.close()
+        self._peers.clear()
 
     # ------------------------------------------------------------ forward
     def forward(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
@@ -101,6 +139,18 @@ class UlyssesAttention:
         scale = head_dim ** -0.5 if scale is None else float(scale)
         k = self.kernels
         with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
+            px = self._peer(geo, dtype, device)
+            if px is not None:
+                status = self._device_status(device)
+                status.poll()
+                out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
+                k.prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, px.dst_blocks, geo, dtype, eps, norm_rope)
+                px.barrier()
+                k.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status)
+                px.barrier()
+                k.unpack_staged(px.staging, out, geo)
+                self._count(state, geo, dtype, "peer")
+                return out
             ws, status = self._workspace(geo, dtype, device)
             status.poll()
             out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
@@ -112,15 +162,28 @@ class UlyssesAttention:
                 k.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status)
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
                 k.unpack(ws["out_recv"], out, geo)
-        if state is not None:
-            qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
-            state["padded_heads"] = geo.padded_heads
-            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
-            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
-            state["out_collectives"] = state.get("out_collectives", 0) + 1
-            state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
-            state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
+        self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local")
         return out
+
+    def _device_status(self, device):
+        if device.index not in self._status:
+            self._status[device.index] = self.kernels.DeviceStatus(device)
+        return self._status[device.index]
+
+    @staticmethod
+    def _count(state, geo, dtype, exchange):
+        """The reference's sequence-state counters (powershard/wan_model.py:441-502):
+        one q/k/v exchange and one output exchange per block, with their bytes."""
+        if state is None:
+            return
+        qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+        state["padded_heads"] = geo.padded_heads
+        state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+        state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
+        state["out_collectives"] = state.get("out_collectives", 0) + 1
+        state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
+        state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
+        state["exchange"] = exchange
 
     def forward_joint(self, txt, img, w_q=None, w_k=None, txt_freqs=None, img_freqs=None, *, total_img: int,
                       heads: int, eps: float = 1e-6, scale: float | None = None,

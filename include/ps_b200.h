@@ -3,11 +3,17 @@
  * provider for ComfyUI-PowerShard.
  *
  * The library (libps_b200.so) holds hand-written CUDA kernels for the three
- * device steps of PowerShard's Ulysses self-attention block; the all-to-all
- * exchanges between them are issued by the host (NCCL through
- * torch.distributed).  Every entry point takes plain device pointers, sizes
- * and a cudaStream_t (as void*), launches asynchronously on that stream and
- * returns a status code; no entry point allocates device memory.
+ * device steps of PowerShard's Ulysses self-attention block.  The two
+ * all-to-all exchanges between them are either issued by the host (NCCL
+ * through torch.distributed, between ps_b200_prepass / ps_b200_ulysses_attn_fwd
+ * / ps_b200_unpack), or fused into the kernels over NVLink peer memory: the
+ * pre-pass stores each destination's block straight into that rank's receive
+ * buffer (ps_b200_prepass_to) and the attention epilogue stores each output
+ * row straight into its owner's staging buffer (ps_b200_ulysses_attn_to);
+ * the host then only orders the steps across ranks (two 4-byte all-reduces).
+ * Every compute entry point takes plain device pointers, sizes and a
+ * cudaStream_t (as void*), launches asynchronously on that stream and returns
+ * a status code; only ps_b200_shared_alloc allocates device memory.
  *
  * Reference interfaces replaced (paths inside the ComfyUI-PowerShard tree):
  *   ps_b200_prepass        powershard/wan_model.py:421-430 (attention_qkv:
@@ -23,6 +29,12 @@
  *                          (wan_model.py:373-376).
  *   ps_b200_unpack         receive-side unpack of ulysses_to_heads,
  *                          powershard/wan_model.py:377-380 / attention.py:93-95.
+ *   ps_b200_prepass_to, ps_b200_ulysses_attn_to, ps_b200_unpack_strided,
+ *   ps_b200_shared_alloc/free, ps_b200_ipc_export/import/close
+ *                          the same steps with the two all_to_all_single calls
+ *                          of wan_model.py:360 and :376 replaced by peer
+ *                          stores (no reference counterpart for the buffer
+ *                          sharing itself: NCCL owns it there).
  *
  * Layout vocabulary: a "segmented" tensor is [batch][segment][row][head][d]
  * with arbitrary element strides for the first four axes and d contiguous.
@@ -32,6 +44,7 @@
 #ifndef PS_B200_H
 #define PS_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -144,6 +157,68 @@ int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, voi
  */
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
                    int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, void* stream);
+
+/*
+ * Unpack with explicit input strides: head block src, token row i of recv
+ * starts at recv + src*src_stride + i*row_stride elements (head j of the
+ * block at + j*head_dim).  ps_b200_unpack is the case src_stride =
+ * seg_rows*heads_per_rank*head_dim, row_stride = heads_per_rank*head_dim;
+ * the peer-exchange staging buffer [seg_rows][world*heads_per_rank][head_dim]
+ * is src_stride = heads_per_rank*head_dim, row_stride =
+ * world*heads_per_rank*head_dim.
+ */
+int ps_b200_unpack_strided(const void* recv, int64_t src_stride, int64_t row_stride, void* out,
+                           int64_t out_row_stride, int dtype, int out_dtype, int n_local, int heads,
+                           int heads_per_rank, int head_dim, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Peer-memory exchange (one process per GPU, GPUs of one node with NVLink
+ * peer access).  Each rank allocates its receive buffer
+ * [world][3][seg_rows][heads_per_rank][head_dim] and its output staging
+ * buffer [seg_rows][world*heads_per_rank][head_dim] with ps_b200_shared_alloc,
+ * exports them with ps_b200_ipc_export, gathers the peers' handles (any host
+ * transport) and maps them with ps_b200_ipc_import.  Per step:
+ *   ps_b200_prepass_to(dst_blocks[d] = receive buffer of rank d + rank*block)
+ *   -> all ranks' pre-passes finished (a cross-rank barrier on the stream)
+ *   -> ps_b200_ulysses_attn_to(out_blocks[s] = staging buffer of rank s +
+ *      rank*heads_per_rank*head_dim, out_row_stride = world*heads_per_rank*head_dim)
+ *   -> barrier -> ps_b200_unpack_strided(own staging buffer).
+ * The barriers also keep a rank from overwriting a peer buffer that the peer
+ * still reads.  Visibility comes from stream order: a barrier (e.g. a
+ * 4-byte all-reduce) starts after the storing kernel has completed, and a
+ * completed kernel's stores, peer stores included, are visible system-wide.
+ * ---------------------------------------------------------------------- */
+#define PS_B200_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc + zero fill of `bytes` (the allocation base, as IPC requires). */
+int ps_b200_shared_alloc(size_t bytes, void** ptr);
+int ps_b200_shared_free(void* ptr);
+/* Handle (PS_B200_IPC_HANDLE_BYTES bytes) of a ps_b200_shared_alloc buffer. */
+int ps_b200_ipc_export(const void* ptr, unsigned char* handle);
+/* Map a peer's buffer into this process (peer access enabled lazily). */
+int ps_b200_ipc_import(const unsigned char* handle, void** ptr);
+int ps_b200_ipc_close(void* ptr);
+
+/*
+ * ps_b200_prepass with one destination pointer per rank instead of one send
+ * buffer: dst_blocks[d] (16-byte aligned, possibly another GPU's memory)
+ * receives the [3][seg_rows][heads_per_rank][head_dim] block of destination d.
+ */
+int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                       const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                       const float* freqs, int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int world,
+                       int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
+                       int norm_rope, void* stream);
+
+/*
+ * ps_b200_ulysses_attn_fwd with one output pointer per source segment: valid
+ * row i of segment s, head j goes to out_blocks[s] + i*out_row_stride +
+ * j*head_dim elements (out_dtype), possibly another GPU's memory.
+ */
+int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t out_row_stride, int dtype,
+                            int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
+                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, int* status,
+                            void* stream);
 
 /*
  * Self-test of the bounded waits (no counterpart in the reference): one warp

@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def nccl_worker(rank, world, port, report, total, heads):
+def nccl_worker(rank, world, port, report, total, heads, exchange):
     import sys
     if str(ROOT) not in sys.path:
         sys.path.insert(0, str(ROOT))
@@ -42,7 +42,7 @@ def nccl_worker(rank, world, port, report, total, heads):
         wk = torch.rand(heads * 128, generator=g) + 0.5
         freqs = oracle.rope_table_3d((total // 100 + 1, 10, 10), 128)[:, :total]
         a, b = oracle.shard_bounds(total, rank, world)
-        engine = UlyssesAttention()
+        engine = UlyssesAttention(exchange=exchange)
         state = {}
         outs = []
         for _ in range(2):
@@ -56,18 +56,25 @@ def nccl_worker(rank, world, port, report, total, heads):
             rel = float(err.mean() / expected.abs().mean()) if expected.numel() else 0.0
             errs.append((float(err.max()) if err.numel() else 0.0, rel))
         ok = all(e <= 2e-2 and r <= 5e-3 for e, r in errs) and state["kv_collectives"] == 2
-        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank)))
+        ok = ok and state["exchange"] == exchange and torch.equal(outs[0], outs[1])
+        engine.close()
+        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank,
+                                                            exchange=state["exchange"])))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("world,total,heads", [(2, 1000, 40), (2, 37, 5), (4, 1023, 40), (8, 4099, 40),
                                                (3, 300, 24)])
-def test_engine_over_nccl(world, total, heads, tmp_path, cuda_lib):
+def test_engine_over_nccl(world, total, heads, exchange, tmp_path, cuda_lib):
+    """Both exchanges: NCCL all_to_all_single, and the kernels' own NVLink
+    peer stores ordered by 4-byte all-reduces (bit-identical results)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"NOT_RUN: needs {world} GPUs, box has {torch.cuda.device_count()}")
     report = tmp_path / "r"
-    mp.spawn(nccl_worker, args=(world, _free_port(), str(report), total, heads), nprocs=world, join=True)
+    mp.spawn(nccl_worker, args=(world, _free_port(), str(report), total, heads, exchange), nprocs=world,
+             join=True)
     for rank in range(world):
         data = json.loads(Path(f"{report}.{rank}").read_text())
         assert data["ok"], data
