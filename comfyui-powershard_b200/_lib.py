@@ -14,7 +14,7 @@ import torch
 from .contract import UnsupportedAttention
 
 LIB_PATH = Path(__file__).resolve().with_name("lib") / "libps_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 BF16, FP16, FP32 = 0, 1, 2
@@ -35,11 +35,11 @@ SIGNATURES = {
         ctypes.c_void_p, _c_i64p, ctypes.c_void_p, _c_i64p, ctypes.c_void_p, _c_i64p,
         ctypes.c_void_p, _c_i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_float, _c_intp, ctypes.c_void_p]),
+        ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t, _c_intp, ctypes.c_void_p]),
     "ps_b200_ulysses_attn_fwd": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
-        _c_intp, ctypes.c_void_p]),
+        ctypes.c_void_p, ctypes.c_size_t, _c_intp, ctypes.c_void_p]),
     "ps_b200_block_fwd_static": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, ctypes.c_void_p, ctypes.c_void_p,
         ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
@@ -49,7 +49,7 @@ SIGNATURES = {
     "ps_b200_ulysses_joint_attn_fwd": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_float, _c_intp, ctypes.c_void_p]),
+        ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t, _c_intp, ctypes.c_void_p]),
     "ps_b200_unpack": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
@@ -64,13 +64,15 @@ SIGNATURES = {
     "ps_b200_ulysses_attn_to": (ctypes.c_int, [
         ctypes.c_void_p, _c_ptrs, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
-        _c_intp, ctypes.c_void_p]),
+        ctypes.c_void_p, ctypes.c_size_t, _c_intp, ctypes.c_void_p]),
     "ps_b200_shared_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "ps_b200_shared_free": (ctypes.c_int, [ctypes.c_void_p]),
     "ps_b200_ipc_export": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte)]),
     "ps_b200_ipc_import": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_void_p)]),
     "ps_b200_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "ps_b200_kernel_launches": (ctypes.c_ulonglong, []),
 }
+ATTN_WORKSPACE_BYTES = 160 * 2 * 128 * 129 * 4
 IPC_HANDLE_BYTES = 64
 
 _LIB = None

@@ -39,6 +39,7 @@
 // B200, moving part of them to an FMA-pipe polynomial or fusing the row max
 // into the exponential pass made the softmax slower.
 #include "ptx.cuh"
+#include "ps_b200.h"
 #include "internal.h"
 
 #include <cuda_bf16.h>
@@ -99,6 +100,24 @@ enum Err : int {
 // segment, first row and valid rows, without divisions.
 struct KeyCursor {
   int i = 0, seg = 0, row0 = 0;
+  // Position the cursor so that the next call of next() returns tile n.
+  __device__ __forceinline__ void skip(const AttnArgs& a, int n) {
+    const int take = min(n, max(a.pre_tiles - i, 0));
+    i += take;
+    n -= take;
+    while (n > 0) {
+      while (row0 >= a.valid_k[seg] && seg + 1 < a.nsegs_k) {
+        ++seg;
+        row0 = 0;
+      }
+      const int left = (a.valid_k[seg] - row0 + kBlockN - 1) / kBlockN;
+      if (left <= 0) break;
+      const int t = min(n, left);
+      row0 += t * kBlockN;
+      i += t;
+      n -= t;
+    }
+  }
   __device__ __forceinline__ void next(const AttnArgs& a, bool& prefix, int& s, int& r, int& valid) {
     if (i < a.pre_tiles) {
       prefix = true;
@@ -193,12 +212,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int batch = blockIdx.z;
+  // Work unit and key range of this CTA.
+  const int bx = blockIdx.x;
+  const bool partial = bx >= args.full_units;
+  const int nparts = partial ? args.split : 1;
+  const int v_split = partial ? bx - args.full_units : 0;
+  const int unit = partial ? args.full_units + v_split / args.split : bx;
+  const int part = partial ? v_split - (v_split / args.split) * args.split : 0;
+  const int slot = partial ? v_split : 0;
+  const int pair = unit % args.npairs;
+  const int head = (unit / args.npairs) % args.grid_heads;
+  const int batch = unit / args.npairs / args.grid_heads;
   const int kv_head = head / args.group;
-  const int tq0 = blockIdx.x * 2;
+  const int tq0 = pair * 2;
   const int tq1 = tq0 + 1;
-  const int T = args.num_kv_tiles;
+  const int k_begin = part * args.num_kv_tiles / nparts;
+  const int T = (part + 1) * args.num_kv_tiles / nparts - k_begin;
   int* status = args.status;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
@@ -255,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // cannot complete another phase before the producer has loaded the K
       // tile gated on it, so parity waits never alias.
       KeyCursor cur;
+      cur.skip(args, k_begin);
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < T && ok; ++i) {
@@ -374,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     KeyCursor cur;
+    cur.skip(args, k_begin);
     for (int i = 0; i < T; ++i) {
       bool pre_unused;
       int seg_unused, row_unused, valid;
@@ -463,7 +494,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     void* const obase = pre ? args.pre_out : args.seg_out[seg];
     const int64_t* ost = pre ? args.pre_o_stride : args.o_stride;
     const int64_t otile = batch * ost[0] + static_cast<int64_t>(row0) * ost[2] + head * ost[3];
-    if (args.out_fp32) {
+    if (partial) {
+      // One part of a split key range: O / l in fp32 and m + log2(l), merged
+      // by attn_combine_kernel (tcgen05.ld stays warp-collective).
+      if (ok) {
+        float* wrow = args.ws_o + ((static_cast<int64_t>(slot) * 2 + t) * kBlockM + row) * kHeadDim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + 32 * c, o);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(wrow + 32 * c);
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            dst[u] = make_float4(__uint_as_float(o[4 * u + 0]) * inv_l, __uint_as_float(o[4 * u + 1]) * inv_l,
+                                 __uint_as_float(o[4 * u + 2]) * inv_l, __uint_as_float(o[4 * u + 3]) * inv_l);
+        }
+        args.ws_lse[(slot * 2 + t) * kBlockM + row] = l > 0.f ? m + __log2f(l) : -INFINITY;
+      }
+    } else if (args.out_fp32) {
       // tcgen05.ld is warp-collective: every lane loads, only valid rows store.
       if (ok) {
         float* orow = reinterpret_cast<float*>(obase) + otile + static_cast<int64_t>(row) * ost[2];
@@ -532,6 +581,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Merges the split parts of the last wave's units: for each valid query row,
+// out = sum_p w_p o_p / sum_p w_p with w_p = 2^(lse_p - max lse), the
+// log-sum-exp combination of partial softmax results.  One CTA per (unit,
+// query tile); 16 threads per row, 8 columns each.
+template <bool kFp16>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs args) {
+  const int u = blockIdx.x >> 1;
+  const int t = blockIdx.x & 1;
+  const int unit = args.full_units + u;
+  const int pair = unit % args.npairs;
+  const int head = (unit / args.npairs) % args.grid_heads;
+  const int batch = unit / args.npairs / args.grid_heads;
+  const int tq = pair * 2 + t;
+  if (tq >= args.num_q_tiles) return;
+  bool pre;
+  int seg, row0, valid;
+  q_tile(args, tq, pre, seg, row0, valid);
+  void* const obase = pre ? args.pre_out : args.seg_out[seg];
+  const int64_t* ost = pre ? args.pre_o_stride : args.o_stride;
+  const int64_t otile = batch * ost[0] + static_cast<int64_t>(row0) * ost[2] + head * ost[3];
+  const int S = args.split;
+  for (int idx = threadIdx.x; idx < kBlockM * 16; idx += 256) {
+    const int r = idx >> 4;
+    const int c = (idx & 15) * 8;
+    if (r >= valid) continue;
+    float mx = -INFINITY;
+    for (int p = 0; p < S; ++p) mx = fmaxf(mx, args.ws_lse[((u * S + p) * 2 + t) * kBlockM + r]);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float wsum = 0.f;
+    for (int p = 0; p < S; ++p) {
+      const float lse = args.ws_lse[((u * S + p) * 2 + t) * kBlockM + r];
+      const float w = lse == -INFINITY ? 0.f : ex2_approx(lse - mx);
+      wsum += w;
+      const float4* src = reinterpret_cast<const float4*>(
+          args.ws_o + ((static_cast<int64_t>(u * S + p) * 2 + t) * kBlockM + r) * kHeadDim + c);
+      const float4 a0 = src[0], a1 = src[1];
+      acc[0] = fmaf(w, a0.x, acc[0]);
+      acc[1] = fmaf(w, a0.y, acc[1]);
+      acc[2] = fmaf(w, a0.z, acc[2]);
+      acc[3] = fmaf(w, a0.w, acc[3]);
+      acc[4] = fmaf(w, a1.x, acc[4]);
+      acc[5] = fmaf(w, a1.y, acc[5]);
+      acc[6] = fmaf(w, a1.z, acc[6]);
+      acc[7] = fmaf(w, a1.w, acc[7]);
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    const int64_t oidx = otile + static_cast<int64_t>(r) * ost[2] + c;
+    if (args.out_fp32) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(obase) + oidx);
+      dst[0] = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+      dst[1] = make_float4(acc[4] * inv, acc[5] * inv, acc[6] * inv, acc[7] * inv);
+    } else {
+      uint4 v;
+      v.x = pack2<kFp16>(acc[0] * inv, acc[1] * inv);
+      v.y = pack2<kFp16>(acc[2] * inv, acc[3] * inv);
+      v.z = pack2<kFp16>(acc[4] * inv, acc[5] * inv);
+      v.w = pack2<kFp16>(acc[6] * inv, acc[7] * inv);
+      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(obase) + oidx) = v;
+    }
+  }
+}
+
 }  // namespace attn
 
 namespace {
@@ -545,9 +656,13 @@ int prepare_kernel() {
 
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& tqp, const CUtensorMap& tkp, const CUtensorMap& tvp,
-                     const AttnArgs& args, int heads_q, int batch, bool fp16, cudaStream_t stream) {
+                     const AttnArgs& args, int64_t total_units, bool fp16, cudaStream_t stream) {
   using namespace attn;
-  const dim3 grid((args.num_q_tiles + 1) / 2, heads_q, batch);
+  const int64_t split_units = args.split > 1 ? total_units - args.full_units : 0;
+  const int64_t ctas = split_units > 0 ? args.full_units + split_units * args.split : total_units;
+  if (ctas <= 0) return 0;
+  if (ctas > 0x7fffffff) return set_error(PS_B200_ERR_UNSUPPORTED, "attention grid above 2^31 CTAs");
+  const dim3 grid(static_cast<unsigned>(ctas));
   const dim3 block(kThreads);
   if (fp16) {
     if (int rc = prepare_kernel<true>()) return rc;
@@ -556,8 +671,19 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
     if (int rc = prepare_kernel<false>()) return rc;
     attn_fwd_kernel<false><<<grid, block, kSmemBytes, stream>>>(tq, tk, tv, tqp, tkp, tvp, args);
   }
-  const cudaError_t err = cudaGetLastError();
+  cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return set_cuda_error("attention launch", err);
+  count_launch();
+  if (split_units > 0) {
+    const dim3 cgrid(static_cast<unsigned>(split_units * 2));
+    if (fp16)
+      attn_combine_kernel<true><<<cgrid, 256, 0, stream>>>(args);
+    else
+      attn_combine_kernel<false><<<cgrid, 256, 0, stream>>>(args);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return set_cuda_error("attention combine launch", err);
+    count_launch();
+  }
   return 0;
 }
 

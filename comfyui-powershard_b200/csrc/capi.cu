@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -49,6 +50,19 @@ int check_device() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  int sms = 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  return sms;
+}
+
+std::atomic<unsigned long long> g_launches{0};
 
 bool is16bit(int dtype) { return dtype == PS_B200_BF16 || dtype == PS_B200_FP16; }
 
@@ -125,8 +139,8 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
                      const int64_t out_st[4], int dtype, int out_dtype, int batch, int grid_heads, int group,
                      int head_dim,
                      int seg_rows_q, int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k,
-                     float softmax_scale, int* status, void* stream, const Prefix* pre = nullptr,
-                     const int* seg_valid = nullptr, void* const* seg_out = nullptr) {
+                     float softmax_scale, void* workspace, size_t workspace_bytes, int* status, void* stream,
+                     const Prefix* pre = nullptr, const int* seg_valid = nullptr, void* const* seg_out = nullptr) {
   const int pre_len = pre ? pre->len : 0;
   if (segs_q > kMaxSegs || segs_k > kMaxSegs)
     return set_error(PS_B200_ERR_UNSUPPORTED, "more than %d segments", kMaxSegs);
@@ -215,7 +229,30 @@ int attention_common(const SegTensor& q, const SegTensor& k, const SegTensor& v,
   a.num_kv_tiles += a.pre_tiles;
   a.pre_out = pre_len ? pre->out : out;
   for (int i = 0; i < 4; ++i) a.pre_o_stride[i] = pre_len ? pre->out_st[i] : out_st[i];
-  return launch_attention(tq, tk, tv, tqp, tkp, tvp, a, grid_heads, batch, fp16, static_cast<cudaStream_t>(stream));
+  // Work units (tile pair, head, batch).  The last, partial wave's units are
+  // split along the key range when a workspace is given, so that wave ends
+  // about `split` times sooner.
+  a.npairs = (a.num_q_tiles + 1) / 2;
+  a.grid_heads = grid_heads;
+  const int64_t units = int64_t(a.npairs) * grid_heads * batch;
+  a.full_units = static_cast<int>(units < 0x7fffffff ? units : 0x7fffffff);
+  a.split = 1;
+  if (workspace && workspace_bytes >= size_t(kAttnWorkspaceBytes) && aligned16(workspace)) {
+    const int sms = sm_count();
+    const int64_t rem = units % sms;
+    if (rem > 0 && sms <= 160) {
+      int split = static_cast<int>(sms / rem);
+      split = split < kMaxSplit ? split : kMaxSplit;
+      split = split < a.num_kv_tiles / 2 ? split : a.num_kv_tiles / 2;  // at least two key tiles per part
+      if (split >= 2) {
+        a.split = split;
+        a.full_units = static_cast<int>(units - rem);
+        a.ws_o = static_cast<float*>(workspace);
+        a.ws_lse = a.ws_o + rem * split * 2 * 128 * 128;
+      }
+    }
+  }
+  return launch_attention(tq, tk, tv, tqp, tkp, tvp, a, units, fp16, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace
@@ -231,6 +268,8 @@ int set_error(int code, const char* fmt, ...) {
 int set_cuda_error(const char* what, cudaError_t err) {
   return set_error(PS_B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 }  // namespace psb
 
@@ -342,7 +381,7 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
                      const void* v, const int64_t v_strides[4], void* out, const int64_t out_strides[4],
                      int dtype, int out_dtype, int batch, int heads_q, int heads_kv, int head_dim, int seg_rows_q,
                      int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k, float softmax_scale,
-                     int* status, void* stream) {
+                     void* workspace, size_t workspace_bytes, int* status, void* stream) {
   if (!q_strides || !k_strides || !v_strides || !out_strides) return set_error(PS_B200_ERR_INVALID, "null strides");
   if (heads_kv <= 0 || heads_q < 0 || heads_q % heads_kv != 0)
     return set_error(PS_B200_ERR_INVALID, "heads_q must be a positive multiple of heads_kv");
@@ -350,12 +389,14 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
   SegTensor tk{k, {k_strides[0], k_strides[1], k_strides[2], k_strides[3]}, heads_kv};
   SegTensor tv{v, {v_strides[0], v_strides[1], v_strides[2], v_strides[3]}, heads_kv};
   return attention_common(tq, tk, tv, out, out_strides, dtype, out_dtype, batch, heads_q, heads_q / heads_kv, head_dim,
-                          seg_rows_q, segs_q, len_q, seg_rows_k, segs_k, len_k, softmax_scale, status, stream);
+                          seg_rows_q, segs_q, len_q, seg_rows_k, segs_k, len_k, softmax_scale, workspace,
+                          workspace_bytes, status, stream);
 }
 
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
                              int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
-                             float softmax_scale, int* status, void* stream) {
+                             float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                             void* stream) {
   if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
       heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
     return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
@@ -370,13 +411,14 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
   SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows, world, total,
-                          seg_rows, world, total, softmax_scale, status, stream, nullptr, seg_valid);
+                          seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status, stream, nullptr,
+                          seg_valid);
 }
 
 int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t out_row_stride, int dtype,
                             int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
-                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, int* status,
-                            void* stream) {
+                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, void* workspace,
+                            size_t workspace_bytes, int* status, void* stream) {
   if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
       heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
     return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
@@ -394,14 +436,15 @@ int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t o
   SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
   return attention_common(tq, tk, tv, nullptr, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
-                          world, total, seg_rows, world, total, softmax_scale, status, stream, nullptr, seg_valid,
-                          out_blocks);
+                          world, total, seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status,
+                          stream, nullptr, seg_valid, out_blocks);
 }
 
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
                                    int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
                                    const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
-                                   float softmax_scale, int* status, void* stream) {
+                                   float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                                   void* stream) {
   if (world < 1 || seg_rows < 1 || total < 1 || prefix_len < 0 || heads_per_rank < 1 || heads_valid < 0 ||
       heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
     return set_error(PS_B200_ERR_INVALID, "inconsistent joint Ulysses geometry");
@@ -431,7 +474,8 @@ int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, voi
     pre.out_st[3] = D;
   }
   return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
-                          world, total, seg_rows, world, total, softmax_scale, status, stream, &pre, seg_valid);
+                          world, total, seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status,
+                          stream, &pre, seg_valid);
 }
 
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,
@@ -473,6 +517,8 @@ int ps_b200_unpack_strided(const void* recv, int64_t src_stride, int64_t row_str
   a.out_fp32 = out_dtype == PS_B200_FP32;
   return launch_unpack(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
 }
+
+unsigned long long ps_b200_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 // ---------------------------------------------------------------- shared buffers
 int ps_b200_shared_alloc(size_t bytes, void** ptr) {

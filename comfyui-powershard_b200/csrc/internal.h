@@ -34,11 +34,30 @@ struct AttnArgs {
   int pre_tiles;         // ceil(pre_len / 128)
   void* pre_out;         // prefix output row 0, head 0
   int64_t pre_o_stride[4];  // batch, (unused), row, head strides in elements
+  // Work units: (query tile pair, head, batch), pair fastest; the grid is 1-D.
+  // Units [0, full_units) run whole; each later unit (the last, partial wave)
+  // runs as `split` CTAs over consecutive parts of the key range, writing
+  // partials that attn_combine_kernel merges.
+  int npairs;            // ceil(num_q_tiles / 2)
+  int grid_heads;
+  int full_units;
+  int split;             // 1: no split
+  float* ws_o;           // [slot][2][128][128] fp32: O / l of one part, slot = (unit - full_units) * split + part
+  float* ws_lse;         // [slot][2][128] fp32: m + log2(l) of one part (log2 units of the scaled scores)
 };
 
+constexpr int kMaxSplit = 8;
+// Workspace bytes for up to 160 SMs: one partial (O, lse) per CTA of a wave.
+constexpr int64_t kAttnWorkspaceBytes = int64_t(160) * 2 * 128 * (128 + 1) * 4;
+
+// Launches the attention grid (full_units + split units * split CTAs) and,
+// when units are split, the combine kernel after it on the same stream.
 int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                      const CUtensorMap& tqp, const CUtensorMap& tkp, const CUtensorMap& tvp,
-                     const AttnArgs& args, int heads_q, int batch, bool fp16, cudaStream_t stream);
+                     const AttnArgs& args, int64_t total_units, bool fp16, cudaStream_t stream);
+
+// Process-wide count of kernels this library launched (ps_b200_kernel_launches).
+void count_launch();
 
 struct PrepassArgs {
   const void* x[3];        // q, k, v projection outputs, [n_local][heads*head_dim]

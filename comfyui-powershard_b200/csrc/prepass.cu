@@ -243,7 +243,9 @@ int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
   else
     prepass_kernel<false><<<grid, block, 0, stream>>>(a);
   const cudaError_t err = cudaGetLastError();
-  return err == cudaSuccess ? 0 : set_cuda_error("prepass launch", err);
+  if (err != cudaSuccess) return set_cuda_error("prepass launch", err);
+  count_launch();
+  return 0;
 }
 
 int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream) {
@@ -263,7 +265,9 @@ int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream) {
     else unpack_kernel<false, false><<<blocks, kUnpackThreads, 0, stream>>>(a);
   }
   const cudaError_t err = cudaGetLastError();
-  return err == cudaSuccess ? 0 : set_cuda_error("unpack launch", err);
+  if (err != cudaSuccess) return set_cuda_error("unpack launch", err);
+  count_launch();
+  return 0;
 }
 
 }  // namespace psb

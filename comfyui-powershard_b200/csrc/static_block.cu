@@ -80,7 +80,7 @@ extern "C" int ps_b200_block_fwd_static(const void* x_q, const void* x_k, const 
                                qkv, dtype, 1, n, n, heads, heads, head_dim, eps, 1, stream))
     return rc;
   if (int rc = ps_b200_ulysses_attn_fwd(qkv, out, dtype, out_dtype, 1, n, n, nullptr, heads, heads, head_dim,
-                                        softmax_scale, status, stream))
+                                        softmax_scale, nullptr, 0, status, stream))
     return rc;
   if (host_status) {
     err = cudaMemcpyAsync(host_status, status, sizeof(int), cudaMemcpyDeviceToHost, s);

@@ -139,12 +139,27 @@ def prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, dst_blocks, geo: UlyssesGeometry,
     _lib.check(rc, "ps_b200_prepass_to")
 
 
+def attention_workspace(device: torch.device) -> torch.Tensor:
+    """Scratch for the attention entry points (split last wave); one per
+    stream of concurrent calls."""
+    return torch.empty(_lib.ATTN_WORKSPACE_BYTES, dtype=torch.uint8, device=device)
+
+
+def _ws(workspace):
+    if workspace is None:
+        return None, 0
+    if workspace.device.type != "cuda" or not workspace.is_contiguous():
+        raise ValueError("attention workspace must be a contiguous CUDA tensor")
+    return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+
+
 def _seg_table(geo: UlyssesGeometry):
     """Per-segment row table for the C ABI: None for ceil-width shards."""
     return _lib.i32(geo.sizes) if geo.sizes is not None else None
 
 
-def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status: DeviceStatus | None):
+def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status: DeviceStatus | None,
+                      workspace=None):
     """Attention over the receive buffer [W,3,width,h,D] for this rank's real heads."""
     lib = _lib.load()
     _check16(recv, "attention recv")
@@ -158,7 +173,7 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
     rc = lib.ps_b200_ulysses_attn_fwd(
         recv.data_ptr(), out_send.data_ptr(), _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype),
         geo.world, geo.width, geo.total, _seg_table(geo), geo.heads_per_rank, geo.heads_valid, geo.head_dim,
-        float(scale),
+        float(scale), *_ws(workspace),
         status.ptr if status is not None else None, _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_attn_fwd")
     if status is not None:
@@ -166,7 +181,7 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
 
 
 def ulysses_joint_attention(recv, prefix_qkv, out_send, prefix_out, geo: UlyssesGeometry, scale: float,
-                            status: DeviceStatus | None):
+                            status: DeviceStatus | None, workspace=None):
     """Joint attention: this rank's text rows prefix_qkv [3,P,h,D] ahead of the
     image rows of recv [W,3,width,h,D]; text outputs -> prefix_out [P,h,D],
     image outputs -> out_send [W,width,h,D]."""
@@ -188,7 +203,8 @@ def ulysses_joint_attention(recv, prefix_qkv, out_send, prefix_out, geo: Ulysses
     rc = lib.ps_b200_ulysses_joint_attn_fwd(
         recv.data_ptr(), prefix_qkv.data_ptr(), out_send.data_ptr(), prefix_out.data_ptr(),
         _lib.dtype_code(recv.dtype), _lib.dtype_code(out_send.dtype), geo.world, geo.width, geo.total, plen,
-        _seg_table(geo), h, geo.heads_valid, d, float(scale), status.ptr if status is not None else None,
+        _seg_table(geo), h, geo.heads_valid, d, float(scale), *_ws(workspace),
+        status.ptr if status is not None else None,
         _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_joint_attn_fwd")
     if status is not None:
@@ -213,7 +229,7 @@ def unpack(out_recv, out, geo: UlyssesGeometry):
 
 
 def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch.dtype, geo: UlyssesGeometry,
-                         scale: float, status: DeviceStatus | None):
+                         scale: float, status: DeviceStatus | None, workspace=None):
     """``ulysses_attention`` storing segment s's valid rows at the device
     address ``out_blocks[s]`` (row stride ``out_row_stride`` elements, head j
     at + j*D): each source rank's staging buffer, the fused output exchange."""
@@ -228,7 +244,7 @@ def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch
     rc = lib.ps_b200_ulysses_attn_to(
         recv.data_ptr(), _lib.ptrs(out_blocks), int(out_row_stride), _lib.dtype_code(recv.dtype),
         _lib.dtype_code(out_dtype), geo.world, geo.width, geo.total, _seg_table(geo), geo.heads_per_rank,
-        geo.heads_valid, geo.head_dim, float(scale), status.ptr if status is not None else None,
+        geo.heads_valid, geo.head_dim, float(scale), *_ws(workspace), status.ptr if status is not None else None,
         _lib.stream_handle(recv.device))
     _lib.check(rc, "ps_b200_ulysses_attn_to")
     if status is not None:
@@ -255,7 +271,7 @@ def unpack_staged(staging, out, geo: UlyssesGeometry):
     _lib.check(rc, "ps_b200_unpack_strided")
 
 
-def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None):
+def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None, workspace=None):
     """softmax(Q K^T * scale) V for BLHD tensors (GQA by head grouping)."""
     lib = _lib.load()
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
@@ -272,7 +288,7 @@ def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None):
     rc = lib.ps_b200_attn_fwd(
         q.data_ptr(), st(q), k.data_ptr(), st(k), v.data_ptr(), st(v), out.data_ptr(), st(out),
         _lib.dtype_code(q.dtype), _lib.dtype_code(out.dtype), b, hq, hk, d,
-        lq, 1, lq, lk, 1, lk, float(scale), status.ptr if status is not None else None,
+        lq, 1, lq, lk, 1, lk, float(scale), *_ws(workspace), status.ptr if status is not None else None,
         _lib.stream_handle(q.device))
     _lib.check(rc, "ps_b200_attn_fwd")
     if status is not None:

@@ -35,6 +35,7 @@ class B200Provider:
         self.identity = _lib.library_identity()
         self.identity["provider"] = NAME
         self._status = {}
+        self._workspaces = {}
 
     def _status_for(self, device: torch.device) -> ops.DeviceStatus:
         key = device.index if device.index is not None else torch.cuda.current_device()
@@ -70,8 +71,16 @@ class B200Provider:
         scale = q.shape[-1] ** -0.5 if o.softmax_scale is None else float(o.softmax_scale)
         out = torch.empty(q.shape[:-1] + (v.shape[-1],), dtype=q.dtype, device=q.device)
         with torch.cuda.device(q.device):
-            ops.attention_blhd(q, k, v, out, scale, status)
+            ops.attention_blhd(q, k, v, out, scale, status, self._workspace_for(q.device))
         return out
+
+    def _workspace_for(self, device):
+        """Attention scratch per (device, current stream)."""
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        ws = self._workspaces.get(key)
+        if ws is None:
+            ws = self._workspaces[key] = ops.attention_workspace(device)
+        return ws
 
 
 def _tma_ok(t: torch.Tensor) -> bool:

@@ -60,6 +60,7 @@ class UlyssesAttention:
         self._buffers = {}
         self._status = {}
         self._peers = {}
+        self._attn_ws = {}
 
     # ------------------------------------------------------------ topology
     def world_rank(self):
@@ -146,7 +147,8 @@ class UlyssesAttention:
                 out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
                 k.prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, px.dst_blocks, geo, dtype, eps, norm_rope)
                 px.barrier()
-                k.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status)
+                k.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status,
+                                       **self._ws(device))
                 px.barrier()
                 k.unpack_staged(px.staging, out, geo)
                 self._count(state, geo, dtype, "peer")
@@ -157,13 +159,23 @@ class UlyssesAttention:
             k.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope)
             self._exchange(ws["recv"], ws["send"], geo)
             if geo.world == 1:
-                k.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status)
+                k.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status, **self._ws(device))
             else:
-                k.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status)
+                k.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status, **self._ws(device))
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
                 k.unpack(ws["out_recv"], out, geo)
         self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local")
         return out
+
+    def _ws(self, device) -> dict:
+        """Keyword argument with the attention workspace of (device, stream)
+        for the CUDA kernels; stand-in kernels take none."""
+        if self.kernels is not ops or device.type != "cuda":
+            return {}
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        if key not in self._attn_ws:
+            self._attn_ws[key] = ops.attention_workspace(device)
+        return {"workspace": self._attn_ws[key]}
 
     def _device_status(self, device):
         if device.index not in self._status:
@@ -243,9 +255,10 @@ class UlyssesAttention:
             prefix = tb["send"][geo.rank]
             if geo.world == 1:
                 k.ulysses_joint_attention(ws["recv"], prefix, img_out.view(geo.out_shape()), txt_out, geo, scale,
-                                          status)
+                                          status, **self._ws(device))
             else:
-                k.ulysses_joint_attention(ws["recv"], prefix, ws["out_send"], tb["out"], geo, scale, status)
+                k.ulysses_joint_attention(ws["recv"], prefix, ws["out_send"], tb["out"], geo, scale, status,
+                                          **self._ws(device))
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
                 k.unpack(ws["out_recv"], img_out, geo)
                 if plen:

@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define PS_B200_ABI_VERSION 1
+#define PS_B200_ABI_VERSION 2
 
 /* Return codes. */
 #define PS_B200_OK 0
@@ -69,6 +69,23 @@ extern "C" {
  * output is undefined and the host must raise).  0 means success. */
 #define PS_B200_DEVICE_TIMEOUT_FIRST 101
 #define PS_B200_DEVICE_TIMEOUT_LAST 199
+
+/*
+ * Attention workspace.  Every attention entry point takes an optional device
+ * workspace (16-byte aligned, >= PS_B200_ATTN_WORKSPACE_BYTES; NULL or smaller
+ * disables its use).  With one, the units of work of the last, partial wave
+ * (a unit is two 128-row query tiles of one head) are split along the key
+ * range over several CTAs whose partial results (O / l in fp32 and the
+ * log-sum-exp of each row) a second kernel merges, so that wave finishes
+ * sooner; results equal the unsplit computation up to fp32 rounding.  The
+ * workspace is scratch owned by one call at a time: calls that may overlap
+ * on the GPU need separate workspaces.  Size: one partial per CTA of a wave
+ * for up to 160 SMs.
+ */
+#define PS_B200_ATTN_WORKSPACE_BYTES (160LL * 2 * 128 * 129 * 4)
+
+/* Kernels this library has launched in this process (all entry points). */
+unsigned long long ps_b200_kernel_launches(void);
 
 /* ABI version of the loaded library (PS_B200_ABI_VERSION). */
 int ps_b200_abi_version(void);
@@ -97,8 +114,8 @@ const char* ps_b200_last_error(void);
  */
 int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
                     const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
-                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local, int seg_rows,
-                    int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream);
+                    const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local,
+                    int seg_rows, int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream);
 
 /*
  * softmax(Q K^T * softmax_scale) V over segmented tensors (BLHD is the case
@@ -112,7 +129,7 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
                      const void* v, const int64_t v_strides[4], void* out, const int64_t out_strides[4],
                      int dtype, int out_dtype, int batch, int heads_q, int heads_kv, int head_dim, int seg_rows_q,
                      int segs_q, int len_q, int seg_rows_k, int segs_k, int len_k, float softmax_scale,
-                     int* status, void* stream);
+                     void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /*
  * Attention over the Ulysses receive buffer recv [world][3][seg_rows][heads_per_rank][head_dim]
@@ -131,7 +148,8 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
  */
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,
                              int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
-                             float softmax_scale, int* status, void* stream);
+                             float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                             void* stream);
 
 /*
  * Joint attention (Flux: text tokens replicated on every rank, image tokens
@@ -148,7 +166,8 @@ int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int ou
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
                                    int dtype, int out_dtype, int world, int seg_rows, int total, int prefix_len,
                                    const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
-                                   float softmax_scale, int* status, void* stream);
+                                   float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                                   void* stream);
 
 /*
  * Inverse unpack: recv [world][seg_rows][heads_per_rank][head_dim] (dtype)
@@ -217,8 +236,8 @@ int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const 
  */
 int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t out_row_stride, int dtype,
                             int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
-                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, int* status,
-                            void* stream);
+                            int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, void* workspace,
+                            size_t workspace_bytes, int* status, void* stream);
 
 /*
  * Self-test of the bounded waits (no counterpart in the reference): one warp

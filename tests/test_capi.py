@@ -33,7 +33,9 @@ def test_exports_every_header_symbol(lib):
 
 
 def test_abi_version(lib):
-    assert lib.ps_b200_abi_version() == 1
+    from powershard_b200 import _lib
+    assert lib.ps_b200_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.ps_b200_kernel_launches() == 0  # nothing launched without a GPU
 
 
 def test_unsupported_dtype_is_reported_before_launch(lib):
@@ -49,7 +51,7 @@ def test_unsupported_head_dim(lib):
     from powershard_b200 import _lib
     st = _lib.i64([0, 0, 128, 64])
     rc = lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 64,
-                              4, 1, 4, 4, 1, 4, 0.1, None, None)
+                              4, 1, 4, 4, 1, 4, 0.1, None, 0, None, None)
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"head_dim" in lib.ps_b200_last_error()
 
@@ -62,11 +64,11 @@ def test_invalid_geometry(lib):
     # empty key set with queries
     st = _lib.i64([0, 0, 128, 128])
     rc = lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
-                              4, 1, 4, 4, 1, 0, 0.1, None, None)
+                              4, 1, 4, 4, 1, 0, 0.1, None, 0, None, None)
     assert rc == _lib.ERR_INVALID
     # misaligned pointer
     rc = lib.ps_b200_attn_fwd(18, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
-                              4, 1, 4, 4, 1, 4, 0.1, None, None)
+                              4, 1, 4, 4, 1, 4, 0.1, None, 0, None, None)
     assert rc == _lib.ERR_INVALID
     assert b"aligned" in lib.ps_b200_last_error()
 
@@ -78,13 +80,13 @@ def test_segment_row_table_is_validated(lib):
     from powershard_b200 import _lib
     ok = _lib.i32([3, 3, 2])  # split_sizes(8, 3)
     assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 3, 3, 8, ok, 2, 0, 128, 0.1,
-                                        None, None) == _lib.OK  # no valid heads: nothing to launch
+                                        None, 0, None, None) == _lib.OK  # no valid heads: nothing to launch
     for bad, total in (([3, 3, 3], 8), ([4, 2, 2], 8), ([3, -1, 6], 8)):
         rc = lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 3, 3, total, _lib.i32(bad), 2, 2, 128,
-                                          0.1, None, None)
+                                          0.1, None, 0, None, None)
         assert rc == _lib.ERR_INVALID, bad
     rc = lib.ps_b200_ulysses_joint_attn_fwd(16, 16, 16, 16, _lib.BF16, _lib.BF16, 3, 3, 8, 4, _lib.i32([4, 2, 2]),
-                                            2, 2, 128, 0.1, None, None)
+                                            2, 2, 128, 0.1, None, 0, None, None)
     assert rc == _lib.ERR_INVALID
     assert b"segment" in lib.ps_b200_last_error()
 
@@ -93,8 +95,8 @@ def test_empty_work_is_a_no_op(lib):
     from powershard_b200 import _lib
     st = _lib.i64([0, 0, 128, 128])
     assert lib.ps_b200_attn_fwd(16, st, 16, st, 16, st, 16, st, _lib.BF16, _lib.BF16, 1, 1, 1, 128,
-                                4, 1, 0, 4, 1, 4, 0.1, None, None) == _lib.OK
-    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 2, 3, 0, None, 2, 2, 128, 0.1, None, None) == _lib.OK
+                                4, 1, 0, 4, 1, 4, 0.1, None, 0, None, None) == _lib.OK
+    assert lib.ps_b200_ulysses_attn_fwd(16, 16, _lib.BF16, _lib.BF16, 2, 3, 0, None, 2, 2, 128, 0.1, None, 0, None, None) == _lib.OK
 
 
 def test_error_mapping_to_reference_exceptions():

@@ -132,6 +132,83 @@ def test_ulysses_attention_fp32_output(cuda_lib, oracle):
     assert_attention_close(out.cpu()[0], oracle.sdpa_fp32(q[None], k[None], v[None], 0.07)[0])
 
 
+def _split_of(units: int, key_tiles: int, sms: int) -> int:
+    """The split the library picks for the last wave (mirror of its plan)."""
+    rem = units % sms
+    if rem == 0:
+        return 1
+    split = min(sms // rem, 8, key_tiles // 2)
+    return split if split >= 2 else 1
+
+
+@pytest.mark.parametrize("total,heads,world,out_dtype", [
+    (1000, 2, 1, torch.bfloat16),    # 8 units: split 4
+    (4099, 3, 1, torch.bfloat16),    # 51 units: split 2
+    (1000, 2, 1, torch.float32),     # fp32 output through the combine kernel
+    (1001, 6, 4, torch.bfloat16),    # 4 source segments, 2 real heads per rank
+    (130, 1, 1, torch.bfloat16),     # 2 key tiles: too few to split
+])
+def test_split_last_wave_matches_oracle(cuda_lib, oracle, total, heads, world, out_dtype):
+    """With a workspace, the last partial wave's units run as several CTAs
+    over parts of the key range and a combine kernel merges them by
+    log-sum-exp: same bound against the oracle, and close to the unsplit
+    launch."""
+    from powershard_b200 import _lib, ops
+    lib = _lib.load()
+    recvs = oracle_recv(oracle, total, heads, world, 21)
+    sms = torch.cuda.get_device_properties(DEV).multi_processor_count
+    for rank in range(world):
+        geo = geometry(total, heads, world, rank)
+        if not geo.heads_valid:
+            continue
+        q_tiles = world * -(-geo.width // 128)
+        key_tiles = sum(-(-v // 128) for v in geo.seg_valid())
+        units = -(-q_tiles // 2) * geo.heads_valid
+        recv = recvs[rank].to(DEV)
+        outs = []
+        for ws in (None, ops.attention_workspace(DEV)):
+            out = torch.zeros(geo.out_shape(), dtype=out_dtype, device=DEV)
+            status = ops.DeviceStatus(DEV)
+            before = lib.ps_b200_kernel_launches()
+            ops.ulysses_attention(recv, out, geo, 128 ** -0.5, status, workspace=ws)
+            status.check()
+            launched = lib.ps_b200_kernel_launches() - before
+            expect_split = ws is not None and _split_of(units, key_tiles, sms) > 1
+            assert launched == (2 if expect_split else 1)
+            outs.append(out.float().cpu())
+        q, k, v = oracle.unpack_qkv(recvs[rank], total)
+        ref = oracle.sdpa_fp32(q[None], k[None], v[None])[0]
+        hv = geo.heads_valid
+        for out in outs:
+            got = out.reshape(world * geo.width, geo.heads_per_rank, 128)[:total, :hv]
+            assert_attention_close(got, ref[:, :hv])
+        # Each part rounds its probabilities to bf16 against its own running
+        # max, so split and unsplit differ at the level of that rounding.
+        diff = (outs[0] - outs[1]).abs()
+        assert float(diff.mean() / outs[0].abs().mean()) <= 2e-3 and float(diff.max()) <= 1e-2
+
+
+def test_split_joint_prefix_matches_oracle(cuda_lib, oracle):
+    """Split last wave with a text prefix range (Flux joint attention)."""
+    from powershard_b200 import ops
+    from powershard_b200.partition import UlyssesGeometry
+    prefix, image, heads = 77, 1001, 2
+    g = torch.Generator().manual_seed(9)
+    full = [torch.randn(prefix + image, heads, 128, generator=g).bfloat16() for _ in range(3)]
+    geo = UlyssesGeometry(image, heads, 128, 1, 0)
+    recv = torch.stack([t[prefix:] for t in full])[None].contiguous().to(DEV)      # [1, 3, image, h, D]
+    pre = torch.stack([t[:prefix] for t in full]).contiguous().to(DEV)             # [3, P, h, D]
+    ref = oracle.sdpa_fp32(*(t.float()[None] for t in full))[0]
+    for ws in (None, ops.attention_workspace(DEV)):
+        out = torch.zeros(geo.out_shape(), dtype=torch.bfloat16, device=DEV)
+        pout = torch.zeros(prefix, heads, 128, dtype=torch.bfloat16, device=DEV)
+        status = ops.DeviceStatus(DEV)
+        ops.ulysses_joint_attention(recv, pre, out, pout, geo, 128 ** -0.5, status, workspace=ws)
+        status.check()
+        assert_attention_close(pout, ref[:prefix])
+        assert_attention_close(out[0], ref[prefix:])
+
+
 @pytest.mark.parametrize("b,lq,lk,hq,hk,dtype,scale", [
     (2, 5, 7, 4, 4, torch.float16, .13), (2, 5, 7, 4, 4, torch.bfloat16, .37), (1, 1, 1, 1, 1, torch.bfloat16, None),
     (1, 300, 300, 3, 3, torch.bfloat16, None), (2, 200, 4099, 4, 2, torch.bfloat16, .05),

@@ -52,7 +52,7 @@ def _existing_path(lib, x, wq, wk, freqs, n, heads):
         wq.data_ptr(), wk.data_ptr(), _lib.FP32, freqs.data_ptr(), freqs.stride(0), send.data_ptr(), _lib.BF16,
         1, n, n, heads, heads, 128, 1e-6, 1, stream), "prepass")
     _lib.check(lib.ps_b200_ulysses_attn_fwd(send.data_ptr(), out.data_ptr(), _lib.BF16, _lib.BF16, 1, n, n, None,
-                                            heads, heads, 128, 128 ** -0.5, status.data_ptr(), stream), "attention")
+                                            heads, heads, 128, 128 ** -0.5, None, 0, status.data_ptr(), stream), "attention")
     torch.cuda.synchronize(DEV)
     assert int(status.item()) == 0
     return out
