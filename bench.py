@@ -240,11 +240,14 @@ def main():
     barrier()
     if args.profile:
         torch.cuda.profiler.start()
+    from powershard_b200 import _lib
+    launches0 = _lib.load().ps_b200_kernel_launches()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
         step(proj)
     t1.record()
+    launches = _lib.load().ps_b200_kernel_launches() - launches0
     barrier()
     if args.profile:
         torch.cuda.profiler.stop()
@@ -307,7 +310,6 @@ def main():
                            f"(128x512 fp32 tiles) for {res['attention_chunks']} of {res['attention_chunks_total']} "
                            f"query chunks of head 0 vs all keys ({res['attention_sample_s']:.1f} s), extrapolated "
                            f"to the layer: {res['seconds_per_layer']:.0f} s/layer"))
-    launches_per_step = 2 + (1 if world > 1 else 0)
     if rank == 0:
         line = dict(
             metric=METRIC, value=flops / (ms * 1e-3) / 1e12, unit=UNIT, n_gpus=world, steps=args.steps,
@@ -321,7 +323,7 @@ def main():
             cpu_baseline=cpu,
             e2e=dict(value=flops / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,
                      h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h),
-            clocks=clock, gpu_launches=launches_per_step * args.steps)
+            clocks=clock, gpu_launches=int(launches))
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
