@@ -1,7 +1,7 @@
 // HBM-bound kernels around the attention: the fused q/k RMSNorm + RoPE +
 // Ulysses pack ("pre-pass") and the receive-side head->sequence unpack.
 //
-// Pre-pass, one CTA per token row of the send segment (seg_rows CTAs):
+// Pre-pass, one CTA of 256 threads per token row of the send segment (seg_rows CTAs):
 //   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)   (RMSNorm over the
 //         full width (Wan, norm_rope 1) or over each head (Flux QK-norm,
 //         norm_rope 2, weight [head_dim] shared by the heads))
@@ -14,6 +14,7 @@
 // zeros (they are the zero padding of the reference's packing).
 // All loads/stores are 16-byte vectors; a token row of q/k stays in registers
 // between the sum-of-squares reduction and the normalisation.
+#include "ps_b200.h"
 #include "internal.h"
 
 #include <cuda_bf16.h>
@@ -22,8 +23,7 @@
 namespace psb {
 namespace pre {
 
-constexpr int kThreads = 128;
-constexpr int kMaxVec = 8;  // 8 vectors of 8 elements per thread: width <= 8192
+constexpr int kThreads = 256;
 
 template <bool kFp16>
 __device__ __forceinline__ float to_f(uint16_t v) {
@@ -63,33 +63,48 @@ __device__ __forceinline__ uint4 pack8(const uint16_t (&e)[8]) {
   return v;
 }
 
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// Sums of two values over the CTA (warp xor-shuffles, then the warp partials
+// in warp order).
+__device__ __forceinline__ float2 block_sum2(float a, float b, float2* red) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  __syncthreads();  // red[] may still be read from the previous call
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_float2(a, b);
   __syncthreads();
-  float s = 0.f;
+  float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int w = 0; w < kThreads / 32; ++w) s += red[w];
+  for (int w = 0; w < kThreads / 32; ++w) {
+    s.x += red[w].x;
+    s.y += red[w].y;
+  }
   return s;
 }
 
-template <bool kFp16>
-__global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs a) {
-  __shared__ float red[kThreads / 32];
+// One CTA per token row.  Every load of the row (q, k and v, kVec 16-byte
+// vectors per thread each) is issued before any arithmetic, so the row's
+// reads are in flight together; v is stored as soon as it arrives, q and k
+// share one block reduction (full-width norm) and one read of the RoPE table.
+template <bool kFp16, int kVec>
+__global__ void __launch_bounds__(kThreads, 3) prepass_kernel(const PrepassArgs a) {
+  __shared__ float2 red[kThreads / 32];
+  __shared__ uint16_t* sdst[kMaxSegs];
   const int i = blockIdx.x;
   const int tid = threadIdx.x;
+  if (tid < a.world) sdst[tid] = static_cast<uint16_t*>(a.dst[tid]);
+  __syncthreads();
   const int D = a.head_dim;
   const int h = a.heads_per_rank;
   const int vph = D >> 3;             // vectors per head
   const int nvec = a.heads * vph;     // vectors per token row
   const int64_t block_elems = static_cast<int64_t>(a.seg_rows) * h * D;  // one [seg_rows][h][D] block
-  auto slot = [&](int kind, int g, int dd) -> uint4* {
+  const int64_t row_off = static_cast<int64_t>(i) * h * D;
+  // Destination of vector (head g, element dd) of kind 0; kinds k add k*block_elems.
+  auto slot0 = [&](int g, int dd) -> uint16_t* {
     const int dst = g / h;
     const int j = g - dst * h;
-    return reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.dst[dst]) + kind * block_elems +
-                                    static_cast<int64_t>(i) * h * D + static_cast<int64_t>(j) * D + dd);
+    return sdst[dst] + row_off + static_cast<int64_t>(j) * D + dd;
   };
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
 
@@ -98,105 +113,133 @@ __global__ void __launch_bounds__(kThreads, 4) prepass_kernel(const PrepassArgs 
     for (int kind = 0; kind < 3; ++kind)
       for (int v = tid; v < total; v += kThreads) {
         const int g = v / vph;
-        *slot(kind, g, (v - g * vph) * 8) = zero;
+        *reinterpret_cast<uint4*>(slot0(g, (v - g * vph) * 8) + kind * block_elems) = zero;
       }
     return;
   }
 
-  const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
-  const bool per_head = a.norm_rope == 2;  // Flux QK-norm: statistic per head, weight [head_dim]
+  int gv[kVec], ddv[kVec];
+  bool live[kVec];
+#pragma unroll
+  for (int u = 0; u < kVec; ++u) {
+    const int v = tid + u * kThreads;
+    live[u] = v < nvec;
+    gv[u] = v / vph;
+    ddv[u] = (v - gv[u] * vph) * 8;
+  }
+  uint4 xv[3][kVec];
 #pragma unroll
   for (int kind = 0; kind < 3; ++kind) {
     const uint16_t* x = static_cast<const uint16_t*>(a.x[kind]) + static_cast<int64_t>(i) * a.x_row_stride[kind];
-    const bool normed = kind < 2 && a.norm_rope;
-    uint4 xv[kMaxVec];
-    float ss[kMaxVec];
 #pragma unroll
-    for (int u = 0; u < kMaxVec; ++u) {
-      const int v = tid + u * kThreads;
-      ss[u] = 0.f;
-      if (v < nvec) {
-        const int g = v / vph;
-        xv[u] = __ldg(reinterpret_cast<const uint4*>(x + g * a.x_head_stride[kind] + (v - g * vph) * 8));
-        if (normed) {
+    for (int u = 0; u < kVec; ++u)
+      if (live[u]) xv[kind][u] = __ldg(reinterpret_cast<const uint4*>(x + gv[u] * a.x_head_stride[kind] + ddv[u]));
+  }
+#pragma unroll
+  for (int u = 0; u < kVec; ++u)
+    if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], ddv[u]) + 2 * block_elems) = xv[2][u];
+
+  if (a.norm_rope) {
+    const bool per_head = a.norm_rope == 2;  // Flux QK-norm: statistic per head, weight [head_dim]
+    float ss[2][kVec];
+#pragma unroll
+    for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+      for (int u = 0; u < kVec; ++u) {
+        ss[kind][u] = 0.f;
+        if (live[u]) {
           uint16_t e[8];
-          unpack8(xv[u], e);
+          unpack8(xv[kind][u], e);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float f = to_f<kFp16>(e[q]);
-            ss[u] = fmaf(f, f, ss[u]);
+            ss[kind][u] = fmaf(f, f, ss[kind][u]);
           }
         }
       }
-    }
-    float r[kMaxVec];
-    if (normed && !per_head) {
-      float tot = 0.f;
+    float r[2][kVec];
+    if (!per_head) {
+      float tq = 0.f, tk = 0.f;
 #pragma unroll
-      for (int u = 0; u < kMaxVec; ++u) tot += ss[u];
-      const float total = block_sum(tot, red);
-      const float mean = __fdiv_rn(total, static_cast<float>(a.heads * D));
-      const float rr = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+      for (int u = 0; u < kVec; ++u) {
+        tq += ss[0][u];
+        tk += ss[1][u];
+      }
+      const float2 total = block_sum2(tq, tk, red);
+      const float width = static_cast<float>(a.heads * D);
+      const float rq = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total.x, width), a.eps)));
+      const float rk = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total.y, width), a.eps)));
 #pragma unroll
-      for (int u = 0; u < kMaxVec; ++u) r[u] = rr;
-    } else if (normed) {
+      for (int u = 0; u < kVec; ++u) {
+        r[0][u] = rq;
+        r[1][u] = rk;
+      }
+    } else {
       // The vph (= D/8, a power of two <= 32) consecutive lanes holding one
       // head reduce their partial sums with xor shuffles.
 #pragma unroll
-      for (int u = 0; u < kMaxVec; ++u) {
-        float t = ss[u];
-        for (int o = vph >> 1; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        const float mean = __fdiv_rn(t, static_cast<float>(D));
-        r[u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-      }
-    }
+      for (int kind = 0; kind < 2; ++kind)
 #pragma unroll
-    for (int u = 0; u < kMaxVec; ++u) {
+        for (int u = 0; u < kVec; ++u) {
+          float t = ss[kind][u];
+          for (int o = vph >> 1; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+          r[kind][u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(D)), a.eps)));
+        }
+    }
+    const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      if (!live[u]) continue;
       const int v = tid + u * kThreads;
-      if (v >= nvec) continue;
-      const int g = v / vph;
-      const int dd = (v - g * vph) * 8;
-      uint4 outv = xv[u];
-      if (normed) {
+      const int dd = ddv[u];
+      const float4* fp = reinterpret_cast<const float4*>(frow) + (dd >> 1);
+      float4 F[4];  // RoPE pairs dd/2 .. dd/2+3 of the head: {F00, F01, F10, F11}
+#pragma unroll
+      for (int p = 0; p < 4; ++p) F[p] = __ldg(fp + p);
+      const int widx = per_head ? dd : v * 8;  // weight element of this vector's first value
+#pragma unroll
+      for (int kind = 0; kind < 2; ++kind) {
         uint16_t e[8];
-        unpack8(xv[u], e);
+        unpack8(xv[kind][u], e);
         float y[8];
-        const int widx = per_head ? dd : v * 8;  // weight element of this vector's first value
         if (a.w_fp32) {
           const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + widx);
           const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
           const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[u]), w[q])));
+            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), w[q])));
         } else {
           uint16_t we[8];
           unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + widx)), we);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[u]), to_f<kFp16>(we[q]))));
+            y[q] = to_f<kFp16>(
+                from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), to_f<kFp16>(we[q]))));
         }
-        // RoPE: pair p of this vector is pair (dd/2 + p) of the head.
-        const float4* fp = reinterpret_cast<const float4*>(frow) + (dd >> 1);
         uint16_t o[8];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const float4 F = __ldg(fp + p);  // {F00, F01, F10, F11}
           const float x0 = y[2 * p], x1 = y[2 * p + 1];
-          o[2 * p] = from_f<kFp16>(__fadd_rn(__fmul_rn(F.x, x0), __fmul_rn(F.y, x1)));
-          o[2 * p + 1] = from_f<kFp16>(__fadd_rn(__fmul_rn(F.z, x0), __fmul_rn(F.w, x1)));
+          o[2 * p] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].x, x0), __fmul_rn(F[p].y, x1)));
+          o[2 * p + 1] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].z, x0), __fmul_rn(F[p].w, x1)));
         }
-        outv = pack8(o);
+        *reinterpret_cast<uint4*>(slot0(gv[u], dd) + kind * block_elems) = pack8(o);
       }
-      *slot(kind, g, dd) = outv;
     }
+  } else {
+#pragma unroll
+    for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+      for (int u = 0; u < kVec; ++u)
+        if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], ddv[u]) + kind * block_elems) = xv[kind][u];
   }
   // Head padding: slots of heads [heads, world*h) are zero.
   const int padded = (a.world * h - a.heads) * vph;
   for (int kind = 0; kind < 3; ++kind)
     for (int v = tid; v < padded; v += kThreads) {
       const int g = a.heads + v / vph;
-      *slot(kind, g, (v % vph) * 8) = zero;
+      *reinterpret_cast<uint4*>(slot0(g, (v % vph) * 8) + kind * block_elems) = zero;
     }
 }
 
@@ -238,10 +281,19 @@ int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
   using namespace pre;
   if (a.seg_rows == 0) return 0;
   const dim3 grid(a.seg_rows), block(kThreads);
-  if (fp16)
-    prepass_kernel<true><<<grid, block, 0, stream>>>(a);
-  else
-    prepass_kernel<false><<<grid, block, 0, stream>>>(a);
+  const int nvec = a.heads * (a.head_dim / 8);
+  const int vec = (nvec + kThreads - 1) / kThreads;  // 1..kMaxVec (width <= 8192 is checked by the caller)
+  switch ((fp16 ? 8 : 0) + vec) {
+    case 1: prepass_kernel<false, 1><<<grid, block, 0, stream>>>(a); break;
+    case 2: prepass_kernel<false, 2><<<grid, block, 0, stream>>>(a); break;
+    case 3: prepass_kernel<false, 3><<<grid, block, 0, stream>>>(a); break;
+    case 4: prepass_kernel<false, 4><<<grid, block, 0, stream>>>(a); break;
+    case 9: prepass_kernel<true, 1><<<grid, block, 0, stream>>>(a); break;
+    case 10: prepass_kernel<true, 2><<<grid, block, 0, stream>>>(a); break;
+    case 11: prepass_kernel<true, 3><<<grid, block, 0, stream>>>(a); break;
+    case 12: prepass_kernel<true, 4><<<grid, block, 0, stream>>>(a); break;
+    default: return set_error(PS_B200_ERR_UNSUPPORTED, "prepass: %d vectors per row", nvec);
+  }
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return set_cuda_error("prepass launch", err);
   count_launch();
