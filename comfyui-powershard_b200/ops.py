@@ -271,6 +271,56 @@ def unpack_staged(staging, out, geo: UlyssesGeometry):
     _lib.check(rc, "ps_b200_unpack_strided")
 
 
+def token_pack(x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local: int, heads: int, head_dim: int, eps: float = 1e-6,
+               norm_rope=True):
+    """Token mode, step 1: RMSNorm + RoPE of this rank's rows into the local
+    block ``qkv`` [3, width, H, D] (all heads; rows n_local..width-1 zero),
+    whose k/v part [2, width, H, D] is what the all-gather moves."""
+    mode = int(norm_rope)
+    lib = _lib.load()
+    _check16(qkv, "token pack")
+    width = qkv.shape[1]
+    if qkv.dim() != 4 or tuple(qkv.shape) != (3, width, heads, head_dim) or not qkv.is_contiguous():
+        raise ValueError(f"token pack: qkv must be contiguous [3, width, {heads}, {head_dim}]")
+    geo = UlyssesGeometry(total=n_local, heads=heads, head_dim=head_dim, world=1, rank=0)
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, qkv.dtype, qkv.device, mode)
+    rc = lib.ps_b200_prepass(
+        *args, qkv.data_ptr(), _lib.dtype_code(qkv.dtype), 1, n_local, width, heads, heads, head_dim,
+        float(eps), mode, _lib.stream_handle(qkv.device))
+    _lib.check(rc, "ps_b200_prepass (token mode)")
+
+
+def token_attention(qkv, kv_all, out, n_local: int, total: int, scale: float, status: DeviceStatus | None,
+                    workspace=None):
+    """Token mode, step 3: this rank's queries qkv[0] (first n_local rows)
+    against the gathered keys/values kv_all [W, 2, width, H, D] (segment s
+    holds rank s's shard_bounds rows) -> out [n_local, H, D] directly."""
+    lib = _lib.load()
+    _check16(qkv, "token attention q")
+    _check16(kv_all, "token attention kv")
+    _lib.require_cuda(out, "token attention out")
+    _, width, heads, d = qkv.shape
+    world = kv_all.shape[0]
+    if tuple(kv_all.shape) != (world, 2, width, heads, d) or not kv_all.is_contiguous():
+        raise ValueError(f"token attention: kv_all must be contiguous [W, 2, {width}, {heads}, {d}]")
+    if tuple(out.shape) != (n_local, heads, d) or not out.is_contiguous() or out.dtype not in (qkv.dtype,
+                                                                                            torch.float32):
+        raise ValueError(f"token attention: out must be contiguous [{n_local}, {heads}, {d}]")
+    row, seg = heads * d, 2 * width * heads * d
+    q_st = _lib.i64([0, 0, row, d])
+    kv_st = _lib.i64([0, seg, row, d])
+    o_st = _lib.i64([0, 0, row, d])
+    esize = kv_all.element_size()
+    rc = lib.ps_b200_attn_fwd(
+        qkv.data_ptr(), q_st, kv_all.data_ptr(), kv_st, kv_all.data_ptr() + width * row * esize, kv_st,
+        out.data_ptr(), o_st, _lib.dtype_code(qkv.dtype), _lib.dtype_code(out.dtype), 1, heads, heads, d,
+        width, 1, n_local, width, world, total, float(scale), *_ws(workspace),
+        status.ptr if status is not None else None, _lib.stream_handle(qkv.device))
+    _lib.check(rc, "ps_b200_attn_fwd (token mode)")
+    if status is not None:
+        status.arm()
+
+
 def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None, workspace=None):
     """softmax(Q K^T * scale) V for BLHD tensors (GQA by head grouping)."""
     lib = _lib.load()

@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .partition import UlyssesGeometry
+from .partition import UlyssesGeometry, shard_bounds
 
 
 class UlyssesAttention:
@@ -196,6 +196,60 @@ class UlyssesAttention:
         state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
         state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
         state["exchange"] = exchange
+
+    def forward_token(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
+                      eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
+                      norm_rope: bool = True, state: dict | None = None) -> torch.Tensor:
+        """Token mode (the reference's sequence_mode="token",
+        powershard/wan_model.py:489-500): keys/values of every rank are
+        all-gathered, queries stay local, so no output exchange is needed.
+
+        Same inputs and output as ``forward``; rank r owns rows
+        shard_bounds(total, r, W).  Steps: pre-pass into the local block
+        [3, width, H, D]; all-gather of its k/v part into [W, 2, width, H, D]
+        (the rows of gather_tokens, wan_model.py:336-340 / attention.py:40-54,
+        padded to equal width); attention of the local queries against the W
+        key segments, written straight to the [n, H, D] output.
+        """
+        device = x_q.device
+        dtype = x_q.dtype
+        head_dim = x_q.shape[-1] if x_q.dim() == 3 else x_q.shape[-1] // heads
+        world, rank = self.world_rank()
+        a, b = shard_bounds(total, rank, world)
+        n = b - a
+        if x_q.shape[0] != n:
+            raise ValueError("token mode: local token count does not match shard_bounds")
+        width = -(-total // world)
+        out_dtype = out_dtype or dtype
+        scale = head_dim ** -0.5 if scale is None else float(scale)
+        k = self.kernels
+        with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
+            status = self._device_status(device)
+            status.poll()
+            stream = torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else 0
+            key = ("token", device.index, stream, world, width, heads, head_dim, dtype)
+            tb = self._buffers.get(key)
+            if tb is None:
+                tb = self._buffers[key] = dict(
+                    qkv=torch.empty((3, width, heads, head_dim), dtype=dtype, device=device),
+                    kv_all=torch.empty((world if world > 1 else 0, 2, width, heads, head_dim), dtype=dtype,
+                                       device=device))
+            k.token_pack(x_q, x_k, x_v, w_q, w_k, freqs, tb["qkv"], n, heads, head_dim, eps, norm_rope)
+            if world > 1:
+                kv = tb["kv_all"]
+                dist.all_gather_into_tensor(kv.view(world * 2 * width, heads, head_dim),
+                                            tb["qkv"][1:].view(2 * width, heads, head_dim), group=self.group)
+            else:
+                kv = tb["qkv"][1:].unsqueeze(0)  # one segment: this rank's own rows
+            out = torch.empty((n, heads, head_dim), dtype=out_dtype, device=device)
+            k.token_attention(tb["qkv"], kv, out, n, total, scale, status, **self._ws(device))
+        if state is not None:
+            esize = torch.tensor([], dtype=dtype).element_size()
+            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + 2 * total * heads * head_dim * esize
+            state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
+            state["exchange"] = "nccl" if world > 1 else "local"
+        return out
 
     def forward_joint(self, txt, img, w_q=None, w_k=None, txt_freqs=None, img_freqs=None, *, total_img: int,
                       heads: int, eps: float = 1e-6, scale: float | None = None,

@@ -8,6 +8,10 @@
   powershard/wan_model.py:441-502 for callers that already produced
   normalised, rotated q/k (the pre-pass then only packs).
 
+Both follow the shared state's mode: Ulysses (``ulysses`` true, the
+default) or token mode (K/V all-gathered, local queries,
+wan_model.py:489-500).
+
 Both read the module attributes the reference installs
 (``install_wan_compute``, wan_model.py:727-768): ``num_heads``,
 ``head_dim``, ``_ps_sequence`` (the shared state dict: ``enabled``,
@@ -45,8 +49,6 @@ def _state(module) -> dict:
 
 
 def _check_supported(module, state):
-    if state.get("enabled") and not state.get("ulysses", True):
-        raise UnsupportedAttention("b200: token mode (K/V all-gather) is not provided; use sequence_mode='ulysses'")
     if getattr(module, "_ps_main", False) and state.get("ref_attn_masks") is not None:
         raise UnsupportedAttention("b200: InfiniteTalk reference attention maps are not provided")
 
@@ -78,13 +80,16 @@ def self_attention_forward(self, x, freqs, transformer_options=None):
         w_q, w_k = w_q.float(), w_k.float()
     eps = self.norm_q.eps if self.norm_q.eps is not None else 1e-6
     q_lin, k_lin, v_lin = self.q(x), self.k(x), self.v(x)
+    token = state.get("enabled") and not state.get("ulysses", True)
     outs = []
     for b in range(batch):
-        outs.append(engine.forward(
+        run = engine.forward_token if token else engine.forward
+        extra = {} if token else {"local": not state.get("enabled")}
+        outs.append(run(
             _rows(q_lin[b], heads, dim, WIRE_DTYPE), _rows(k_lin[b], heads, dim, WIRE_DTYPE),
             _rows(v_lin[b], heads, dim, WIRE_DTYPE), w_q.contiguous(), w_k.contiguous(), table,
-            total=total, heads=heads, eps=eps, norm_rope=True, local=not state.get("enabled"),
-            state=state if (b == 0 and state.get("enabled")) else None))
+            total=total, heads=heads, eps=eps, norm_rope=True,
+            state=state if (b == 0 and state.get("enabled")) else None, **extra))
     out = torch.stack(outs)
     return self.o(out.reshape(batch, n, heads * dim).to(x.dtype if x.is_floating_point() else out.dtype))
 
@@ -103,9 +108,10 @@ def sequence_attention(self, q, k, v, total=None):
         return out.float()
     total = total or state["total"]
     engine = _engine(self)
+    run = engine.forward if state.get("ulysses", True) else engine.forward_token
     outs = []
     for b in range(batch):
-        outs.append(engine.forward(
+        outs.append(run(
             _rows(q[b], heads, dim, WIRE_DTYPE), _rows(k[b], heads, dim, WIRE_DTYPE),
             _rows(v[b], heads, dim, WIRE_DTYPE), total=total, heads=heads, norm_rope=False,
             out_dtype=torch.float32, state=state if b == 0 else None))

@@ -10,7 +10,8 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its
 Parity pinning: ``tests/golden/make_golden.py`` imported the reference
 package from its source tree and recorded its outputs (RMSNorm, rope_apply,
 attention_qkv, ulysses_to_sequence / ulysses_to_heads over emulated
-collectives, math_attention, sequence_attention, image_parallel's
+collectives, math_attention, sequence_attention in Ulysses and token mode,
+image_parallel's
 SequenceAttention over an image_layout.Layout) as fixtures under
 ``tests/golden/``; ``tests/test_oracle_golden.py`` checks every function here
 against them.  One piece is NOT pinned: the 3-D RoPE *table*
@@ -31,7 +32,8 @@ import torch.nn.functional as F
 __all__ = [
     "shard_bounds", "rms_norm", "rope_apply", "rope_axes", "rope_table_3d",
     "rope_table_flux", "attention_qkv", "pack_qkv", "exchange", "unpack_qkv",
-    "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention",
+    "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention", "gather_rows",
+    "token_sequence_attention",
     "rms_norm_heads", "flux_joint_attention", "split_sizes", "image_local_ranges",
     "image_sequence_attention", "time_reference_sample",
 ]
@@ -290,6 +292,50 @@ def sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: in
         outs.append(pack_out(o.to(wire_dtype), total, world))
     back = exchange(outs)
     return [unpack_out(back[r], total, heads, r, world)[None] for r in range(world)]
+
+
+def gather_rows(parts, total: int, world: int):
+    """All-gather of token rows (powershard/attention.py:40-54): each rank's
+    rows padded to ceil(total/W), concatenated in rank order, sliced to total."""
+    width = math.ceil(total / world)
+    padded = []
+    for p in parts:
+        z = p.new_zeros((width,) + tuple(p.shape[1:]))
+        z[:p.shape[0]] = p
+        padded.append(z)
+    return torch.cat(padded)[:total]
+
+
+def token_sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: int, eps: float = 1e-6,
+                             attention="sdpa", scale=None, provider_dtype=None):
+    """Token-mode self-attention of one block (sequence_mode="token"), ranks
+    simulated: per rank attention_qkv of its rows (powershard/wan_model.py:
+    421-430), k/v of every rank gathered (gather_tokens, :336-340, over
+    gather_rows), run_attention (:398-418) of the local queries against all
+    keys (:489-500).  Returns per rank the fp32 output [1, n_r, H, D];
+    provider_dtype as in ``sequence_attention``."""
+    total = q_lin.shape[1]
+    local = []
+    for r in range(world):
+        a, b = shard_bounds(total, r, world)
+        local.append(attention_qkv(q_lin[:, a:b], k_lin[:, a:b], v_lin[:, a:b], wq, wk, freqs[:, a:b], heads, eps))
+    k = gather_rows([t[1][0] for t in local], total, world)[None]
+    v = gather_rows([t[2][0] for t in local], total, world)[None]
+    fn = sdpa_fp32 if attention == "sdpa" else math_attention
+    outs = []
+    for r in range(world):
+        q = local[r][0]
+        if q.shape[1] == 0:
+            outs.append(q.new_zeros(q.shape, dtype=torch.float32))
+            continue
+        if provider_dtype is None:
+            outs.append(fn(q.float(), k.float(), v.float(), scale))
+        else:
+            sv = _power2_scale(v.float().abs().amax() / 16384.0)
+            o = fn(q.float().to(provider_dtype), k.float().to(provider_dtype),
+                   (v.float() / sv).to(provider_dtype), scale)
+            outs.append(o.to(provider_dtype).float() * sv)
+    return outs
 
 
 # ------------------------------------------------- Flux joint attention

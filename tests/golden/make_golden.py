@@ -18,7 +18,8 @@ inputs + outputs with torch.save next to this script:
   ulysses_to_heads at D=128.
 * ``math_attention.pt`` - attention_contract.math_attention cases.
 * ``sequence_attention.pt`` - wan_model.sequence_attention (Ulysses, math
-  provider, fp32 wire) for W in {1,2,3} on a 40-token, 5-head, D=128 layer.
+  provider, fp32 wire) for W in {1,2,3} on a 40-token, 5-head, D=128 layer;
+  ``sequence_attention_token.pt`` the same in token mode (K/V all-gather).
 * ``image_sequence_attention.pt`` - image_parallel.SequenceAttention (the
   Flux/Qwen attention override: local queries, all-gathered keys/values)
   over image_layout.Layout for uneven image segments, W in {2,3,5}, with a
@@ -189,8 +190,9 @@ def main():
     wq = torch.rand(heads * dim, generator=g) + 0.5
     wk = torch.rand(heads * dim, generator=g) + 0.5
     freqs = rope_table(n_total, dim // 2, 3)
-    for world in (1, 2, 3):
-        cfg = DistributedConfig(attention_backend="math", sequence_mode="ulysses")
+    tcases = []
+    for mode, world in [("ulysses", w) for w in (1, 2, 3)] + [("token", w) for w in (1, 2, 3)]:
+        cfg = DistributedConfig(attention_backend="math", sequence_mode=mode)
 
         def rank_fn(rank):
             a, b = shard_bounds(n_total, rank, world)
@@ -212,9 +214,12 @@ def main():
             return dict(bounds=(a, b), out=out, counters=counters)
         with emulated_collectives(world) as run:
             per_rank = run(rank_fn)
-        scases.append(dict(world=world, heads=heads, total=n_total, dim=dim, ranks=per_rank))
+        (scases if mode == "ulysses" else tcases).append(dict(world=world, heads=heads, total=n_total, dim=dim,
+                                                              ranks=per_rank))
     torch.save(dict(q_lin=q_lin, k_lin=k_lin, v_lin=v_lin, wq=wq, wk=wk, freqs=freqs, eps=1e-6,
                     cases=scases), HERE / "sequence_attention.pt")
+    torch.save(dict(q_lin=q_lin, k_lin=k_lin, v_lin=v_lin, wq=wq, wk=wk, freqs=freqs, eps=1e-6,
+                    cases=tcases), HERE / "sequence_attention_token.pt")
     # ---------------------------------------- image Layout SequenceAttention
     from powershard import image_parallel
     from powershard.image_layout import Layout

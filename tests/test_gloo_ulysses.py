@@ -72,6 +72,28 @@ class OracleKernels:
         from oracle import ulysses_oracle as oracle
         out.copy_(oracle.unpack_out(out_recv, geo.total, geo.heads, geo.rank, geo.world).to(out.dtype))
 
+    @staticmethod
+    def token_pack(x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local, heads, head_dim, eps=1e-6, norm_rope=True):
+        from oracle import ulysses_oracle as oracle
+        if norm_rope:
+            q, k, v = oracle.attention_qkv(x_q[None], x_k[None], x_v[None], w_q, w_k, freqs[None, :, None], heads,
+                                           eps)
+            q, k, v = q[0], k[0], v[0]
+        else:
+            q, k, v = (t.reshape(n_local, heads, head_dim) for t in (x_q, x_k, x_v))
+        qkv.zero_()
+        for kind, t in enumerate((q, k, v)):
+            qkv[kind, :n_local] = t.to(qkv.dtype)
+
+    @staticmethod
+    def token_attention(qkv, kv_all, out, n_local, total, scale, status, workspace=None):
+        from oracle import ulysses_oracle as oracle
+        world = kv_all.shape[0]
+        sizes = [b - a for a, b in (oracle.shard_bounds(total, s, world) for s in range(world))]
+        k = torch.cat([kv_all[s, 0, :n] for s, n in enumerate(sizes)])
+        v = torch.cat([kv_all[s, 1, :n] for s, n in enumerate(sizes)])
+        out.copy_(oracle.sdpa_fp32(qkv[0, :n_local][None], k[None], v[None], scale)[0].to(out.dtype))
+
 
 class LayoutKernels(OracleKernels):
     """Stand-ins driven by the geometry alone (any token split, including the
@@ -152,6 +174,39 @@ def test_image_sequence_attention_over_gloo(world, prefix, image, heads, batch, 
     report = tmp_path / "report.json"
     mp.spawn(image_layout_worker, args=(world, str(tmp_path / "store"), str(report), prefix, image, heads, batch,
                                         skip), nprocs=world, join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
+
+
+def token_worker(rank, world, store, report, total, heads):
+    oracle = _setup_paths()
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        x, wq, wk, freqs = _inputs(total, heads, oracle)
+        a, b = oracle.shard_bounds(total, rank, world)
+        engine = UlyssesAttention(kernels=OracleKernels)
+        state = {}
+        expected = oracle.token_sequence_attention(x[0], x[1], x[2], wq, wk, freqs, heads, world)[rank][0]
+        for step in range(2):  # the second step reuses the cached token buffers
+            out = engine.forward_token(x[0][0, a:b], x[1][0, a:b], x[2][0, a:b], wq, wk, freqs[0, a:b, 0],
+                                       total=total, heads=heads, state=state)
+            torch.testing.assert_close(out, expected, atol=1e-5, rtol=1e-5)
+        assert state["kv_collectives"] == 2 and "out_collectives" not in state
+        assert state["kv_gathered_bytes"] == 2 * 2 * total * heads * 128 * 4
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS")))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads", [(2, 41, 5), (3, 41, 3), (4, 9, 2)])
+def test_token_mode_over_gloo(world, total, heads, tmp_path, gloo_available):
+    """sequence_mode="token": one K/V all-gather per block, local queries, no output exchange."""
+    report = tmp_path / "report.json"
+    mp.spawn(token_worker, args=(world, str(tmp_path / "store"), str(report), total, heads), nprocs=world,
+             join=True)
     assert json.loads(report.read_text())["status"] == "PASS"
 
 

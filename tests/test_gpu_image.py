@@ -10,13 +10,9 @@ emulated on one GPU by threads whose collectives are in-process copies
 Tolerance: max |err| <= 2e-2 and mean |err| / mean |ref| <= 5e-3 against
 the fp32 oracle.
 """
-import threading
-from concurrent.futures import ThreadPoolExecutor
-from contextlib import contextmanager
-
 import pytest
 import torch
-import torch.distributed as dist
+from emulated_dist import emulated_group
 
 pytestmark = pytest.mark.gpu
 
@@ -107,51 +103,6 @@ def test_joint_attention_with_balanced_segments(cuda_lib, oracle, prefix, image,
 
 
 # ------------------------------------------------ override, ranks emulated
-@contextmanager
-def emulated_group(world):
-    """torch.distributed replaced by an in-process thread-per-rank transport."""
-    local = threading.local()
-    barrier = threading.Barrier(world, timeout=120)
-    slots = [None] * world
-    names = ("is_initialized", "get_world_size", "get_rank", "all_to_all_single", "all_gather_into_tensor")
-    saved = {n: getattr(dist, n) for n in names}
-
-    def all_to_all(output, input, group=None):
-        slots[local.rank] = input.clone()
-        barrier.wait()
-        output.copy_(torch.stack([slots[s][local.rank] for s in range(world)]))
-        barrier.wait()
-
-    def all_gather(output, input, group=None):
-        slots[local.rank] = input.clone()
-        barrier.wait()
-        output.copy_(torch.cat(slots).view(output.shape))
-        barrier.wait()
-
-    dist.is_initialized = lambda: True
-    dist.get_world_size = lambda group=None: world
-    dist.get_rank = lambda group=None: local.rank
-    dist.all_to_all_single = all_to_all
-    dist.all_gather_into_tensor = all_gather
-
-    def run(fn):
-        def worker(rank):
-            local.rank = rank
-            torch.cuda.set_device(DEV)
-            try:
-                return fn(rank)
-            except BaseException:
-                barrier.abort()
-                raise
-        with ThreadPoolExecutor(max_workers=world) as ex:
-            return list(ex.map(worker, range(world)))
-    try:
-        yield run
-    finally:
-        for n, f in saved.items():
-            setattr(dist, n, f)
-
-
 def _local(oracle, t, segments, world, rank, heads, skip):
     """Rank's local rows of a full [B, L, H, D] tensor in the block layout."""
     rows = [i for s, e in oracle.image_local_ranges(segments, world, rank) for i in range(s, e)]

@@ -165,3 +165,18 @@ def test_product_image_layout_matches_oracle(oracle, golden_dir):
             geo = UlyssesGeometry(total=split, heads=5, head_dim=128, world=world, rank=r, sizes=lay.sizes)
             assert geo.width == lay.chunk and geo.seg_valid() == lay.sizes
             assert geo.bounds == (lay.a - lay.split_start, lay.b - lay.split_start)
+
+
+@pytest.mark.parametrize("index", range(3))
+def test_token_sequence_attention_matches_reference(oracle, golden_dir, index):
+    """sequence_mode="token": K/V all-gathered, local queries (math provider, fp32 wire)."""
+    data = load(golden_dir, "sequence_attention_token.pt")
+    case = data["cases"][index]
+    outs = oracle.token_sequence_attention(data["q_lin"], data["k_lin"], data["v_lin"], data["wq"], data["wk"],
+                                           data["freqs"], case["heads"], case["world"], data["eps"],
+                                           attention="math", provider_dtype=torch.float16)
+    for r, ref in enumerate(case["ranks"]):
+        torch.testing.assert_close(outs[r], ref["out"], atol=1e-6, rtol=1e-5)
+        assert ref["counters"]["kv_collectives"] == 1 and ref["counters"]["out_collectives"] == 0
+        # gathered bytes: the reference gathers [1, total, 2, H, D] in the fp32 wire
+        assert ref["counters"]["kv_gathered_bytes"] == 2 * case["total"] * case["heads"] * case["dim"] * 4
