@@ -14,7 +14,7 @@ import torch
 from .contract import UnsupportedAttention
 
 LIB_PATH = Path(__file__).resolve().with_name("lib") / "libps_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 BF16, FP16, FP32 = 0, 1, 2
@@ -30,7 +30,7 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, _c_i64p,
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64,
         ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "ps_b200_attn_fwd": (ctypes.c_int, [
         ctypes.c_void_p, _c_i64p, ctypes.c_void_p, _c_i64p, ctypes.c_void_p, _c_i64p,
         ctypes.c_void_p, _c_i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -60,7 +60,7 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, _c_i64p, _c_i64p,
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64,
         _c_ptrs, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "ps_b200_ulysses_attn_to": (ctypes.c_int, [
         ctypes.c_void_p, _c_ptrs, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,

@@ -281,7 +281,7 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                    const float* freqs, int64_t freqs_row_stride, void* const* dst, int dtype,
                    int world, int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
-                   int norm_rope, void* stream) {
+                   int norm_rope, int rope_style, int rope_pairs, void* stream) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
   if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
       int64_t(heads_per_rank) * world < heads || head_dim <= 0)
@@ -290,6 +290,16 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
   if (norm_rope < 0 || norm_rope > 2) return set_error(PS_B200_ERR_INVALID, "norm_rope must be 0, 1 or 2");
   if (norm_rope == 2 && (head_dim / 8 > 32 || ((head_dim / 8) & (head_dim / 8 - 1)) != 0))
     return set_error(PS_B200_ERR_UNSUPPORTED, "per-head norm needs head_dim/8 a power of two <= 32");
+  if (rope_style != 0 && rope_style != 1) return set_error(PS_B200_ERR_INVALID, "rope_style must be 0 or 1");
+  if (norm_rope && rope_style == 0 && rope_pairs != head_dim / 2)
+    return set_error(PS_B200_ERR_INVALID, "interleaved RoPE rotates head_dim/2 pairs (got %d)", rope_pairs);
+  if (norm_rope && rope_style == 1) {
+    if (rope_pairs <= 0 || rope_pairs % 8 != 0 || 2 * rope_pairs > head_dim)
+      return set_error(PS_B200_ERR_UNSUPPORTED, "split-half RoPE needs rope_pairs a positive multiple of 8, "
+                                                "2*rope_pairs <= head_dim (got %d)", rope_pairs);
+    if (head_dim / 8 > 32 || ((head_dim / 8) & (head_dim / 8 - 1)) != 0)
+      return set_error(PS_B200_ERR_UNSUPPORTED, "split-half RoPE needs head_dim/8 a power of two <= 32");
+  }
   if (int64_t(heads) * head_dim > 8192)
     return set_error(PS_B200_ERR_UNSUPPORTED, "heads*head_dim above 8192 is not supported");
   if (seg_rows == 0) return PS_B200_OK;
@@ -333,6 +343,8 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
   a.head_dim = head_dim;
   a.eps = eps;
   a.norm_rope = norm_rope;
+  a.rope_style = rope_style;
+  a.rope_pairs = rope_pairs;
   return launch_prepass(a, dtype == PS_B200_FP16, static_cast<cudaStream_t>(stream));
 }
 
@@ -347,7 +359,7 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
                     const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                     const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local,
                     int seg_rows, int heads, int heads_per_rank, int head_dim, float eps, int norm_rope,
-                    void* stream) {
+                    int rope_style, int rope_pairs, void* stream) {
   if (world < 1 || world > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "world must be in [1, %d]", kMaxSegs);
   if (!send || !aligned16(send)) {
     if (seg_rows > 0) return set_error(PS_B200_ERR_INVALID, "send buffer null or not 16-byte aligned");
@@ -357,14 +369,14 @@ int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int
   for (int d = 0; d < world; ++d) dst[d] = static_cast<char*>(send) + d * block;
   return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
                         freqs_row_stride, dst, dtype, world, n_local, seg_rows, heads, heads_per_rank, head_dim,
-                        eps, norm_rope, stream);
+                        eps, norm_rope, rope_style, rope_pairs, stream);
 }
 
 int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
                        const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                        const float* freqs, int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int world,
                        int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
-                       int norm_rope, void* stream) {
+                       int norm_rope, int rope_style, int rope_pairs, void* stream) {
   if (world < 1 || world > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "world must be in [1, %d]", kMaxSegs);
   if (seg_rows > 0) {
     if (!dst_blocks) return set_error(PS_B200_ERR_INVALID, "null destination table");
@@ -374,7 +386,7 @@ int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const 
   }
   return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
                         freqs_row_stride, dst_blocks, dtype, world, n_local, seg_rows, heads, heads_per_rank,
-                        head_dim, eps, norm_rope, stream);
+                        head_dim, eps, norm_rope, rope_style, rope_pairs, stream);
 }
 
 int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],

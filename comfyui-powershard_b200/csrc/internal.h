@@ -72,6 +72,8 @@ struct PrepassArgs {
   int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
   float eps;
   int norm_rope;           // 0: plain pack, 1: full-width RMSNorm + RoPE, 2: per-head RMSNorm + RoPE
+  int rope_style;          // 0: interleaved pairs (2j, 2j+1) over the head; 1: split half (j, j+rope_pairs)
+  int rope_pairs;          // rotated pairs per head (head_dim/2 for style 0; a multiple of 8 for style 1)
 };
 
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);

@@ -3,9 +3,11 @@
 //
 // Pre-pass, one CTA of 256 threads per token row of the send segment (seg_rows CTAs):
 //   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)   (RMSNorm over the
-//         full width (Wan, norm_rope 1) or over each head (Flux QK-norm,
+//         full width (Wan, norm_rope 1) or over each head (Flux / H3 QK-norm,
 //         norm_rope 2, weight [head_dim] shared by the heads))
-//         out[2j], out[2j+1] = F[j] @ (y[2j], y[2j+1])     (interleaved RoPE)
+//         out[2j], out[2j+1] = F[j] @ (y[2j], y[2j+1])     (interleaved RoPE, style 0)
+//         out[j], out[j+P]   = F[j] @ (y[j], y[j+P]), j < P (split-half partial
+//         RoPE of H3, style 1; elements >= 2P keep y)
 //   v   : copied.
 // Each result goes straight to its slot of the all-to-all send buffer
 // [world][3][seg_rows][heads_per_rank][head_dim]: global head g lands in
@@ -86,8 +88,8 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float2* red) {
 // vectors per thread each) is issued before any arithmetic, so the row's
 // reads are in flight together; v is stored as soon as it arrives, q and k
 // share one block reduction (full-width norm) and one read of the RoPE table.
-template <bool kFp16, int kVec>
-__global__ void __launch_bounds__(kThreads, 3) prepass_kernel(const PrepassArgs a) {
+template <bool kFp16, int kVec, bool kSplit>
+__global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(const PrepassArgs a) {
   __shared__ float2 red[kThreads / 32];
   __shared__ uint16_t* sdst[kMaxSegs];
   const int i = blockIdx.x;
@@ -187,44 +189,95 @@ __global__ void __launch_bounds__(kThreads, 3) prepass_kernel(const PrepassArgs 
         }
     }
     const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
+    constexpr bool split = kSplit;  // split-half partial RoPE (H3); else interleaved pairs
+    const int half_vec = a.rope_pairs >> 3;  // split style: vectors between an element and its partner
+    const int lane = tid & 31;
 #pragma unroll
     for (int u = 0; u < kVec; ++u) {
-      if (!live[u]) continue;
       const int v = tid + u * kThreads;
       const int dd = ddv[u];
-      const float4* fp = reinterpret_cast<const float4*>(frow) + (dd >> 1);
-      float4 F[4];  // RoPE pairs dd/2 .. dd/2+3 of the head: {F00, F01, F10, F11}
-#pragma unroll
-      for (int p = 0; p < 4; ++p) F[p] = __ldg(fp + p);
       const int widx = per_head ? dd : v * 8;  // weight element of this vector's first value
+      // Split style: the vector holding elements dd..dd+7 pairs with the one
+      // rope_pairs elements away, half_vec lanes up or down in the same warp.
+      const bool first = split && dd < a.rope_pairs;
+      const bool second = split && !first && dd < 2 * a.rope_pairs;
+      const int partner_lane = first ? lane + half_vec : (second ? lane - half_vec : lane);
+      const int pair0 = split ? (first ? dd : dd - a.rope_pairs) : (dd >> 1);
+      const bool rotate = !split || first || second;
+      float4 F[4];  // interleaved style: pairs pair0..pair0+3, {F00, F01, F10, F11}, read once for q and k
+      if (!split && live[u]) {
+        const float4* fp = reinterpret_cast<const float4*>(frow) + pair0;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) F[p] = __ldg(fp + p);
+      }
 #pragma unroll
       for (int kind = 0; kind < 2; ++kind) {
         uint16_t e[8];
         unpack8(xv[kind][u], e);
         float y[8];
-        if (a.w_fp32) {
-          const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + widx);
-          const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
-          const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        if (live[u]) {
+          if (a.w_fp32) {
+            const float4* wp = reinterpret_cast<const float4*>(static_cast<const float*>(a.w[kind]) + widx);
+            const float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), w[q])));
+            for (int q = 0; q < 8; ++q)
+              y[q] = to_f<kFp16>(from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), w[q])));
+          } else {
+            uint16_t we[8];
+            unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + widx)), we);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              y[q] = to_f<kFp16>(
+                  from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), to_f<kFp16>(we[q]))));
+          }
         } else {
-          uint16_t we[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.w[kind]) + widx)), we);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            y[q] = to_f<kFp16>(
-                from_f<kFp16>(__fmul_rn(__fmul_rn(to_f<kFp16>(e[q]), r[kind][u]), to_f<kFp16>(we[q]))));
+          for (int q = 0; q < 8; ++q) y[q] = 0.f;
         }
         uint16_t o[8];
+        if (!split) {
+          if (live[u]) {
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const float x0 = y[2 * p], x1 = y[2 * p + 1];
-          o[2 * p] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].x, x0), __fmul_rn(F[p].y, x1)));
-          o[2 * p + 1] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].z, x0), __fmul_rn(F[p].w, x1)));
+            for (int p = 0; p < 4; ++p) {
+              const float x0 = y[2 * p], x1 = y[2 * p + 1];
+              o[2 * p] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].x, x0), __fmul_rn(F[p].y, x1)));
+              o[2 * p + 1] = from_f<kFp16>(__fadd_rn(__fmul_rn(F[p].z, x0), __fmul_rn(F[p].w, x1)));
+            }
+          }
+        } else {
+          // Exchange the normalised (16-bit exact) values with the partner lane;
+          // every lane takes part in the shuffles.
+          uint16_t yb[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) yb[q] = from_f<kFp16>(y[q]);
+          const uint4 mine = pack8(yb);
+          uint4 other;
+          other.x = __shfl_sync(0xffffffffu, mine.x, partner_lane);
+          other.y = __shfl_sync(0xffffffffu, mine.y, partner_lane);
+          other.z = __shfl_sync(0xffffffffu, mine.z, partner_lane);
+          other.w = __shfl_sync(0xffffffffu, mine.w, partner_lane);
+          uint16_t pb[8];
+          unpack8(other, pb);
+          if (live[u]) {
+            if (rotate) {
+              const float4* fp = reinterpret_cast<const float4*>(frow) + pair0;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 M = __ldg(fp + q);
+                // first half: out_j = M00 x_j + M01 x_{j+P}; second half: out_{j+P} = M10 x_j + M11 x_{j+P}
+                const float xj = first ? y[q] : to_f<kFp16>(pb[q]);
+                const float xp = first ? to_f<kFp16>(pb[q]) : y[q];
+                o[q] = first ? from_f<kFp16>(__fadd_rn(__fmul_rn(M.x, xj), __fmul_rn(M.y, xp)))
+                             : from_f<kFp16>(__fadd_rn(__fmul_rn(M.z, xj), __fmul_rn(M.w, xp)));
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) o[q] = yb[q];  // past the rotated dims: the normalised value
+            }
+          }
         }
-        *reinterpret_cast<uint4*>(slot0(gv[u], dd) + kind * block_elems) = pack8(o);
+        if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], dd) + kind * block_elems) = pack8(o);
       }
     }
   } else {
@@ -283,15 +336,27 @@ int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
   const dim3 grid(a.seg_rows), block(kThreads);
   const int nvec = a.heads * (a.head_dim / 8);
   const int vec = (nvec + kThreads - 1) / kThreads;  // 1..kMaxVec (width <= 8192 is checked by the caller)
-  switch ((fp16 ? 8 : 0) + vec) {
-    case 1: prepass_kernel<false, 1><<<grid, block, 0, stream>>>(a); break;
-    case 2: prepass_kernel<false, 2><<<grid, block, 0, stream>>>(a); break;
-    case 3: prepass_kernel<false, 3><<<grid, block, 0, stream>>>(a); break;
-    case 4: prepass_kernel<false, 4><<<grid, block, 0, stream>>>(a); break;
-    case 9: prepass_kernel<true, 1><<<grid, block, 0, stream>>>(a); break;
-    case 10: prepass_kernel<true, 2><<<grid, block, 0, stream>>>(a); break;
-    case 11: prepass_kernel<true, 3><<<grid, block, 0, stream>>>(a); break;
-    case 12: prepass_kernel<true, 4><<<grid, block, 0, stream>>>(a); break;
+  const bool split = a.rope_style == 1 && a.norm_rope != 0;
+  switch ((split ? 16 : 0) + (fp16 ? 8 : 0) + vec) {
+#define PSB_PREPASS_CASE(code, FP16, VEC, SPLIT) \
+  case code: prepass_kernel<FP16, VEC, SPLIT><<<grid, block, 0, stream>>>(a); break;
+    PSB_PREPASS_CASE(1, false, 1, false)
+    PSB_PREPASS_CASE(2, false, 2, false)
+    PSB_PREPASS_CASE(3, false, 3, false)
+    PSB_PREPASS_CASE(4, false, 4, false)
+    PSB_PREPASS_CASE(9, true, 1, false)
+    PSB_PREPASS_CASE(10, true, 2, false)
+    PSB_PREPASS_CASE(11, true, 3, false)
+    PSB_PREPASS_CASE(12, true, 4, false)
+    PSB_PREPASS_CASE(17, false, 1, true)
+    PSB_PREPASS_CASE(18, false, 2, true)
+    PSB_PREPASS_CASE(19, false, 3, true)
+    PSB_PREPASS_CASE(20, false, 4, true)
+    PSB_PREPASS_CASE(25, true, 1, true)
+    PSB_PREPASS_CASE(26, true, 2, true)
+    PSB_PREPASS_CASE(27, true, 3, true)
+    PSB_PREPASS_CASE(28, true, 4, true)
+#undef PSB_PREPASS_CASE
     default: return set_error(PS_B200_ERR_UNSUPPORTED, "prepass: %d vectors per row", nvec);
   }
   const cudaError_t err = cudaGetLastError();

@@ -77,7 +77,7 @@ extern "C" int ps_b200_block_fwd_static(const void* x_q, const void* x_k, const 
   cudaError_t err = cudaMemsetAsync(status, 0, sizeof(int), s);
   if (err != cudaSuccess) return set_cuda_error("static block: clearing the status word", err);
   if (int rc = ps_b200_prepass(x_q, x_k, x_v, x_row_strides, nullptr, w_qnorm, w_knorm, w_dtype, freqs, freqs_row_stride,
-                               qkv, dtype, 1, n, n, heads, heads, head_dim, eps, 1, stream))
+                               qkv, dtype, 1, n, n, heads, heads, head_dim, eps, 1, 0, head_dim / 2, stream))
     return rc;
   if (int rc = ps_b200_ulysses_attn_fwd(qkv, out, dtype, out_dtype, 1, n, n, nullptr, heads, heads, head_dim,
                                         softmax_scale, nullptr, 0, status, stream))

@@ -60,7 +60,15 @@ def _check16(t: torch.Tensor, what: str):
 NORM_NONE, NORM_FULL, NORM_PER_HEAD = 0, 1, 2
 
 
-def _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo: UlyssesGeometry, dtype, device, mode: int):
+def _rope_args(head_dim: int, rope_split_pairs):
+    """(style, pairs) for the C ABI: interleaved over the head, or split half."""
+    if rope_split_pairs is None:
+        return 0, head_dim // 2
+    return 1, int(rope_split_pairs)
+
+
+def _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo: UlyssesGeometry, dtype, device, mode: int,
+                    rope_split_pairs=None):
     """Validated pointer / stride arguments shared by the two pre-pass entry points."""
     for t, name in ((x_q, "q"), (x_k, "k"), (x_v, "v")):
         _check16(t, f"prepass {name}")
@@ -91,9 +99,10 @@ def _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo: UlyssesGeometry, dtype,
         wq, wk = w_q.data_ptr(), w_k.data_ptr()
         if freqs.dtype != torch.float32 or freqs.device != device:
             raise ValueError("prepass: freqs must be fp32 on the exchange device")
-        if (freqs.dim() != 4 or freqs.shape[0] != n or tuple(freqs.shape[1:]) != (geo.head_dim // 2, 2, 2)
+        pairs = _rope_args(geo.head_dim, rope_split_pairs)[1]
+        if (freqs.dim() != 4 or freqs.shape[0] != n or tuple(freqs.shape[1:]) != (pairs, 2, 2)
                 or freqs.stride()[1:] != (4, 2, 1) or freqs.stride(0) % 4 != 0):
-            raise ValueError(f"prepass: freqs must be [{n}, {geo.head_dim // 2}, 2, 2] with contiguous rows")
+            raise ValueError(f"prepass: freqs must be [{n}, {pairs}, 2, 2] with contiguous rows")
         fptr, fstride = freqs.data_ptr(), freqs.stride(0)
     return [x_q.data_ptr(), x_k.data_ptr(), x_v.data_ptr(),
             _lib.i64([x_q.stride(0), x_k.stride(0), x_v.stride(0)]), _lib.i64(head_strides),
@@ -101,41 +110,44 @@ def _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo: UlyssesGeometry, dtype,
 
 
 def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: float = 1e-6,
-            norm_rope=True):
+            norm_rope=True, rope_split_pairs=None):
     """RMSNorm(q), RMSNorm(k), RoPE, pack into ``send`` [W,3,width,h,D].
 
     x_*: [n_local, H*D] (row stride may exceed H*D) or [n_local, H, D] with
     any row and head strides (e.g. a [H, L, D] tensor transposed) and unit
     inner stride; freqs: [n_local, D/2, 2, 2] fp32.  norm_rope: False/0 pack
     only, True/1 RMSNorm over the full width (Wan; w_* [H*D]), 2 RMSNorm per
-    head (Flux QK-norm; w_* [D]).
+    head (Flux / H3 QK-norm; w_* [D]).  rope_split_pairs: None rotates
+    interleaved pairs over the whole head (freqs [n, D/2, 2, 2]); P rotates
+    pairs (j, j+P), j < P, and keeps the rest (H3 partial RoPE, freqs
+    [n, P, 2, 2]).
     """
     mode = int(norm_rope)
     lib = _lib.load()
     _check16(send, "prepass send")
     if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
         raise ValueError(f"prepass: send must be contiguous {geo.send_shape()}")
-    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, send.dtype, send.device, mode)
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, send.dtype, send.device, mode, rope_split_pairs)
     rc = lib.ps_b200_prepass(
         *args, send.data_ptr(), _lib.dtype_code(send.dtype),
         geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
-        mode, _lib.stream_handle(send.device))
+        mode, *_rope_args(geo.head_dim, rope_split_pairs), _lib.stream_handle(send.device))
     _lib.check(rc, "ps_b200_prepass")
 
 
 def prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, dst_blocks, geo: UlyssesGeometry, dtype: torch.dtype,
-               eps: float = 1e-6, norm_rope=True):
+               eps: float = 1e-6, norm_rope=True, rope_split_pairs=None):
     """``prepass`` storing destination d's [3,width,h,D] block at the device
     address ``dst_blocks[d]`` (a peer's receive buffer: the fused exchange)."""
     mode = int(norm_rope)
     lib = _lib.load()
     if len(dst_blocks) != geo.world:
         raise ValueError(f"prepass_to: {len(dst_blocks)} destination blocks for {geo.world} ranks")
-    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, dtype, x_q.device, mode)
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, dtype, x_q.device, mode, rope_split_pairs)
     rc = lib.ps_b200_prepass_to(
         *args, _lib.ptrs(dst_blocks), _lib.dtype_code(dtype),
         geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
-        mode, _lib.stream_handle(x_q.device))
+        mode, *_rope_args(geo.head_dim, rope_split_pairs), _lib.stream_handle(x_q.device))
     _lib.check(rc, "ps_b200_prepass_to")
 
 
@@ -272,7 +284,7 @@ def unpack_staged(staging, out, geo: UlyssesGeometry):
 
 
 def token_pack(x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local: int, heads: int, head_dim: int, eps: float = 1e-6,
-               norm_rope=True):
+               norm_rope=True, rope_split_pairs=None):
     """Token mode, step 1: RMSNorm + RoPE of this rank's rows into the local
     block ``qkv`` [3, width, H, D] (all heads; rows n_local..width-1 zero),
     whose k/v part [2, width, H, D] is what the all-gather moves."""
@@ -283,10 +295,10 @@ def token_pack(x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local: int, heads: int, he
     if qkv.dim() != 4 or tuple(qkv.shape) != (3, width, heads, head_dim) or not qkv.is_contiguous():
         raise ValueError(f"token pack: qkv must be contiguous [3, width, {heads}, {head_dim}]")
     geo = UlyssesGeometry(total=n_local, heads=heads, head_dim=head_dim, world=1, rank=0)
-    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, qkv.dtype, qkv.device, mode)
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, qkv.dtype, qkv.device, mode, rope_split_pairs)
     rc = lib.ps_b200_prepass(
         *args, qkv.data_ptr(), _lib.dtype_code(qkv.dtype), 1, n_local, width, heads, heads, head_dim,
-        float(eps), mode, _lib.stream_handle(qkv.device))
+        float(eps), mode, *_rope_args(head_dim, rope_split_pairs), _lib.stream_handle(qkv.device))
     _lib.check(rc, "ps_b200_prepass (token mode)")
 
 

@@ -120,19 +120,22 @@ class UlyssesAttention:
     # ------------------------------------------------------------ forward
     def forward(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
                 eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
-                norm_rope: bool = True, state: dict | None = None, local: bool = False) -> torch.Tensor:
+                norm_rope: bool = True, state: dict | None = None, local: bool = False,
+                rope_split_pairs: int | None = None) -> torch.Tensor:
         """One block's self-attention for this rank's tokens.
 
         x_q/x_k/x_v: [n_local, H*D] q/k/v projection outputs (bf16/fp16).
         With norm_rope, w_q/w_k [H*D] are the RMSNorm weights and freqs is
         the rank's rotation table [n_local, D/2, 2, 2] fp32; without it the
         inputs are already normalised/rotated and are only exchanged.
+        norm_rope may also be ops.NORM_PER_HEAD (w_q/w_k [D]); rope_split_pairs
+        P selects the split-half partial RoPE of H3 (freqs [n_local, P, 2, 2]).
         Returns [n_local, H, D] in out_dtype (default: the input dtype).
         local=True runs the block on this rank alone (no exchange, W = 1).
         """
         device = x_q.device
         dtype = x_q.dtype
-        head_dim = x_q.shape[-1] // heads
+        head_dim = x_q.shape[-1] if x_q.dim() == 3 else x_q.shape[-1] // heads
         geo = self.geometry(total, heads, head_dim, local)
         if x_q.shape[0] != geo.n_local:
             raise ValueError("Ulysses local token/head geometry mismatch")
@@ -145,7 +148,8 @@ class UlyssesAttention:
                 status = self._device_status(device)
                 status.poll()
                 out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
-                k.prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, px.dst_blocks, geo, dtype, eps, norm_rope)
+                k.prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, px.dst_blocks, geo, dtype, eps, norm_rope,
+                             **self._rope_kw(rope_split_pairs))
                 px.barrier()
                 k.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status,
                                        **self._ws(device))
@@ -156,7 +160,8 @@ class UlyssesAttention:
             ws, status = self._workspace(geo, dtype, device)
             status.poll()
             out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
-            k.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope)
+            k.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope,
+                      **self._rope_kw(rope_split_pairs))
             self._exchange(ws["recv"], ws["send"], geo)
             if geo.world == 1:
                 k.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status, **self._ws(device))
@@ -176,6 +181,10 @@ class UlyssesAttention:
         if key not in self._attn_ws:
             self._attn_ws[key] = ops.attention_workspace(device)
         return {"workspace": self._attn_ws[key]}
+
+    @staticmethod
+    def _rope_kw(rope_split_pairs) -> dict:
+        return {} if rope_split_pairs is None else {"rope_split_pairs": rope_split_pairs}
 
     def _device_status(self, device):
         if device.index not in self._status:
@@ -199,7 +208,8 @@ class UlyssesAttention:
 
     def forward_token(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
                       eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
-                      norm_rope: bool = True, state: dict | None = None) -> torch.Tensor:
+                      norm_rope: bool = True, state: dict | None = None,
+                      rope_split_pairs: int | None = None) -> torch.Tensor:
         """Token mode (the reference's sequence_mode="token",
         powershard/wan_model.py:489-500): keys/values of every rank are
         all-gathered, queries stay local, so no output exchange is needed.
@@ -234,7 +244,8 @@ class UlyssesAttention:
                     qkv=torch.empty((3, width, heads, head_dim), dtype=dtype, device=device),
                     kv_all=torch.empty((world if world > 1 else 0, 2, width, heads, head_dim), dtype=dtype,
                                        device=device))
-            k.token_pack(x_q, x_k, x_v, w_q, w_k, freqs, tb["qkv"], n, heads, head_dim, eps, norm_rope)
+            k.token_pack(x_q, x_k, x_v, w_q, w_k, freqs, tb["qkv"], n, heads, head_dim, eps, norm_rope,
+                         **self._rope_kw(rope_split_pairs))
             if world > 1:
                 kv = tb["kv_all"]
                 dist.all_gather_into_tensor(kv.view(world * 2 * width, heads, head_dim),

@@ -51,7 +51,7 @@
 extern "C" {
 #endif
 
-#define PS_B200_ABI_VERSION 2
+#define PS_B200_ABI_VERSION 3
 
 /* Return codes. */
 #define PS_B200_OK 0
@@ -108,14 +108,21 @@ const char* ps_b200_last_error(void);
  *                  reference's freqs[0, :, 0]), freqs_row_stride in floats.
  *   send           [world][3][seg_rows][heads_per_rank][head_dim] (dtype).
  *   norm_rope      1: RMSNorm over the full width + RoPE on q and k (Wan),
- *                  2: RMSNorm over each head + RoPE (Flux QK-norm), 0: pack only.
+ *                  2: RMSNorm over each head + RoPE (Flux / H3 QK-norm), 0: pack only.
+ *   rope_style     0: interleaved pairs (2j, 2j+1), rope_pairs = head_dim/2
+ *                  (powershard/wan_model.py:325-329); 1: split half, pairs
+ *                  (j, j+rope_pairs) for j < rope_pairs, elements >= 2*rope_pairs
+ *                  unrotated (H3 partial RoPE, powershard/attention.py:98-103;
+ *                  rope_pairs a multiple of 8).  freqs rows hold rope_pairs
+ *                  2x2 matrices.
  * Rows n_local..seg_rows-1 and heads heads..world*heads_per_rank-1 of the
  * send buffer are written as zeros.
  */
 int ps_b200_prepass(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
                     const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                     const float* freqs, int64_t freqs_row_stride, void* send, int dtype, int world, int n_local,
-                    int seg_rows, int heads, int heads_per_rank, int head_dim, float eps, int norm_rope, void* stream);
+                    int seg_rows, int heads, int heads_per_rank, int head_dim, float eps, int norm_rope,
+                    int rope_style, int rope_pairs, void* stream);
 
 /*
  * softmax(Q K^T * softmax_scale) V over segmented tensors (BLHD is the case
@@ -227,7 +234,7 @@ int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const 
                        const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                        const float* freqs, int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int world,
                        int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
-                       int norm_rope, void* stream);
+                       int norm_rope, int rope_style, int rope_pairs, void* stream);
 
 /*
  * ps_b200_ulysses_attn_fwd with one output pointer per source segment: valid

@@ -30,7 +30,7 @@ import torch
 import torch.nn.functional as F
 
 __all__ = [
-    "shard_bounds", "rms_norm", "rope_apply", "rope_axes", "rope_table_3d",
+    "shard_bounds", "rms_norm", "rope_apply", "rope_split_half", "rope_axes", "rope_table_3d",
     "rope_table_flux", "attention_qkv", "pack_qkv", "exchange", "unpack_qkv",
     "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention", "gather_rows",
     "token_sequence_attention",
@@ -76,6 +76,21 @@ def rope_apply(x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
     x_ = x.float().reshape(*x.shape[:-1], x.shape[-1] // 2, 1, 2)
     out = freqs[..., 0] * x_[..., 0] + freqs[..., 1] * x_[..., 1]
     return out.reshape(*x.shape)
+
+
+def rope_split_half(x: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    """H3 partial RoPE: [S,H,D] x [1,S,1,P,2,2] (powershard/attention.py:98-103).
+
+    Element j < P pairs with element j+P: out_j = M00 x_j + M01 x_{j+P},
+    out_{j+P} = M10 x_j + M11 x_{j+P} (fp32), elements >= 2P pass through;
+    the result is cast back to x.dtype.
+    """
+    p = table.shape[-3]
+    m = table[0].float()
+    a, b = x[..., :p].float(), x[..., p:2 * p].float()
+    first = m[..., 0, 0] * a + m[..., 0, 1] * b
+    second = m[..., 1, 0] * a + m[..., 1, 1] * b
+    return torch.cat([first, second, x[..., 2 * p:].float()], -1).to(x.dtype)
 
 
 def rope_axes(head_dim: int):

@@ -11,6 +11,7 @@ inputs + outputs with torch.save next to this script:
 
 * ``attention_qkv.pt``  - operations.RMSNorm + wan_model.rope_apply through
   wan_model.attention_qkv (fp32 and bf16 projections).
+* ``rope_split_half.pt`` - attention.rope_split_half (H3 partial RoPE).
 * ``ulysses_exchange.pt`` - attention.ulysses_heads_to_sequence ->
   math_attention -> ulysses_sequence_to_heads for W in {3,4,5,6}, heads 7 and
   56, 2W+1 tokens, D=8, V*1e6 (the geometry of the reference's own
@@ -131,6 +132,15 @@ def main():
         cases.append(dict(dtype=str(dtype), heads=heads, eps=1e-6, q_lin=q_lin, k_lin=k_lin, v_lin=v_lin,
                           wq=wq, wk=wk, freqs=freqs, q=q, k=k, v=v))
     torch.save(cases, HERE / "attention_qkv.pt")
+
+    # H3 partial RoPE (split half) on bf16 / fp32 rows.
+    rcases = []
+    for dtype, pairs in ((torch.float32, 32), (torch.bfloat16, 64), (torch.bfloat16, 16)):
+        g = torch.Generator().manual_seed(41 + pairs)
+        x = (torch.randn(29, 3, 128, generator=g) * 2.0).to(dtype)
+        table = rope_table(29, pairs, 7 + pairs)
+        rcases.append(dict(x=x, table=table, out=attention.rope_split_half(x, table)))
+    torch.save(rcases, HERE / "rope_split_half.pt")
 
     # ------------------------------------------------------ Ulysses exchange
     exchange = []

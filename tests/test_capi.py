@@ -34,7 +34,7 @@ def test_exports_every_header_symbol(lib):
 
 def test_abi_version(lib):
     from powershard_b200 import _lib
-    assert lib.ps_b200_abi_version() == _lib.ABI_VERSION == 2
+    assert lib.ps_b200_abi_version() == _lib.ABI_VERSION == 3
     assert lib.ps_b200_kernel_launches() == 0  # nothing launched without a GPU
 
 
@@ -42,7 +42,7 @@ def test_unsupported_dtype_is_reported_before_launch(lib):
     from powershard_b200 import _lib
     strides = _lib.i64([0, 0, 0])
     rc = lib.ps_b200_prepass(None, None, None, strides, None, None, None, 0, None, 0, None, _lib.FP32,
-                             1, 0, 0, 1, 1, 128, 1e-6, 1, None)
+                             1, 0, 0, 1, 1, 128, 1e-6, 1, 0, 64, None)
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"bf16" in lib.ps_b200_last_error()
 

@@ -180,3 +180,21 @@ def test_token_sequence_attention_matches_reference(oracle, golden_dir, index):
         assert ref["counters"]["kv_collectives"] == 1 and ref["counters"]["out_collectives"] == 0
         # gathered bytes: the reference gathers [1, total, 2, H, D] in the fp32 wire
         assert ref["counters"]["kv_gathered_bytes"] == 2 * case["total"] * case["heads"] * case["dim"] * 4
+
+
+@pytest.mark.parametrize("index", range(3))
+def test_rope_split_half_matches_reference(oracle, golden_dir, index):
+    """H3 partial RoPE (attention.rope_split_half): pairs (j, j+P), tail unrotated."""
+    case = load(golden_dir, "rope_split_half.pt")[index]
+    got = oracle.rope_split_half(case["x"], case["table"])
+    assert got.dtype == case["out"].dtype
+    # Separate multiply and add per element vs the reference's 2x2 matmul: at
+    # most one fp32 rounding apart before the cast.
+    if case["x"].dtype == torch.float32:
+        torch.testing.assert_close(got, case["out"], atol=1e-6, rtol=1e-6)
+    else:
+        diff = (got.float() - case["out"].float()).abs()
+        assert float((diff > 0).float().mean()) < 0.01
+        assert float(diff.max()) <= float(case["out"].float().abs().max()) * 2 ** -7
+    p = case["table"].shape[-3]
+    assert torch.equal(got[..., 2 * p:], case["x"][..., 2 * p:])

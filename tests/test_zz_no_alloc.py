@@ -50,7 +50,7 @@ def _existing_path(lib, x, wq, wk, freqs, n, heads):
     _lib.check(lib.ps_b200_prepass(
         x[0].data_ptr(), x[1].data_ptr(), x[2].data_ptr(), _lib.i64([t.stride(0) for t in x]), None,
         wq.data_ptr(), wk.data_ptr(), _lib.FP32, freqs.data_ptr(), freqs.stride(0), send.data_ptr(), _lib.BF16,
-        1, n, n, heads, heads, 128, 1e-6, 1, stream), "prepass")
+        1, n, n, heads, heads, 128, 1e-6, 1, 0, 64, stream), "prepass")
     _lib.check(lib.ps_b200_ulysses_attn_fwd(send.data_ptr(), out.data_ptr(), _lib.BF16, _lib.BF16, 1, n, n, None,
                                             heads, heads, 128, 128 ** -0.5, None, 0, status.data_ptr(), stream), "attention")
     torch.cuda.synchronize(DEV)
