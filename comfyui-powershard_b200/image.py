@@ -106,6 +106,19 @@ class SequenceAttention:
         batch, length, head_dim = q.shape[0], lay.local_len, 128
         prefix = lay.split_start
         out = torch.empty((batch, length, heads, head_dim), dtype=q.dtype, device=q.device)
+        if world == 1 and self.engine.kernels is ops:
+            # One rank holds the whole sequence: attend the caller's tensors in
+            # place (strided TMA maps), no packing.
+            from .provider import _tma_ok
+            qv, kv, vv = (t.transpose(1, 2) if skip else t.unflatten(-1, (heads, head_dim)) for t in (q, k, v))
+            qv, kv, vv = (t if _tma_ok(t) else t.contiguous() for t in (qv, kv, vv))
+            with torch.cuda.device(q.device):
+                status = self.engine._device_status(q.device)
+                status.poll()
+                ops.attention_blhd(qv, kv, vv, out, head_dim ** -0.5, status,
+                                   self.engine._ws(q.device).get("workspace"))
+            return out.permute(0, 2, 1, 3) if kwargs.get("skip_output_reshape", False) else \
+                out.view(batch, length, heads * head_dim)
         for b in range(batch):
             qb, kb, vb = (self._rows(t, b, heads, skip) for t in (q, k, v))
             self.engine.forward_joint(
