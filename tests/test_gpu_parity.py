@@ -132,6 +132,35 @@ def test_ulysses_attention_fp32_output(cuda_lib, oracle):
     assert_attention_close(out.cpu()[0], oracle.sdpa_fp32(q[None], k[None], v[None], 0.07)[0])
 
 
+@pytest.mark.parametrize("slope", [0.5, 4.0, 12.0, -6.0])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_running_max_rescale_paths(cuda_lib, oracle, slope, out_dtype):
+    """Scores that grow (or shrink) steadily along the keys: the row max rises
+    by `slope` log2 units per 32 keys, so the softmax raises its running max
+    inside key tiles at every chunk position - before the first half of P is
+    released, and after it (where O is scaled once that half's PV has run)."""
+    from powershard_b200 import ops
+    total, heads = 1000, 2
+    geo = geometry(total, heads, 1, 0)
+    g = torch.Generator().manual_seed(31)
+    u = torch.randn(128, generator=g)
+    u = u / u.norm()
+    # q . k / sqrt(D) * log2(e) = slope / 32 per key step along the direction u
+    step = slope / 32 / math.log2(math.e) * math.sqrt(128)
+    q = (u * 4.0).expand(total, heads, 128).clone() + 0.05 * torch.randn(total, heads, 128, generator=g)
+    pos = torch.arange(total, dtype=torch.float32)[:, None, None]
+    k = u * (pos * step / 4.0) + 0.05 * torch.randn(total, heads, 128, generator=g)
+    v = torch.randn(total, heads, 128, generator=g)
+    recv = torch.stack([q, k, v])[None].bfloat16()           # [1, 3, total, h, D]
+    out = torch.zeros(geo.out_shape(), dtype=out_dtype, device=DEV)
+    status = ops.DeviceStatus(DEV)
+    ops.ulysses_attention(recv.to(DEV), out, geo, 128 ** -0.5, status, workspace=ops.attention_workspace(DEV))
+    status.check()
+    qb, kb, vb = (t.float() for t in recv[0])
+    ref = oracle.sdpa_fp32(qb[None], kb[None], vb[None])[0]
+    assert_attention_close(out.cpu()[0], ref)
+
+
 def _split_of(units: int, key_tiles: int, sms: int) -> int:
     """The split the library picks for the last wave (mirror of its plan)."""
     rem = units % sms
