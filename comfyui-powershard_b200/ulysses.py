@@ -296,7 +296,8 @@ class UlyssesAttention:
         with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
             ws, status = self._workspace(geo, dtype, device)
             status.poll()
-            tkey = ("txt", device.index, plen, geo.world, geo.heads_per_rank, head_dim, dtype)
+            stream = torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else 0
+            tkey = ("txt", device.index, stream, plen, geo.world, geo.heads_per_rank, head_dim, dtype)
             if tkey not in self._buffers:  # text rows: packed q/k/v and this rank's heads' outputs (wire dtype)
                 self._buffers[tkey] = dict(
                     send=torch.empty(tgeo.send_shape(), dtype=dtype, device=device),
