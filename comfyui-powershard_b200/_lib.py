@@ -71,6 +71,11 @@ SIGNATURES = {
     "ps_b200_ipc_import": (ctypes.c_int, [ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_void_p)]),
     "ps_b200_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
     "ps_b200_kernel_launches": (ctypes.c_ulonglong, []),
+    "ps_b200_ulysses_joint_attn_to": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, _c_ptrs, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t, _c_intp, ctypes.c_void_p]),
+    "ps_b200_broadcast": (ctypes.c_int, [_c_ptrs, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
 }
 ATTN_WORKSPACE_BYTES = 160 * 2 * 128 * 129 * 4
 IPC_HANDLE_BYTES = 64

@@ -349,6 +349,51 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
 }
 
 
+// Shared body of the joint (prefix + segmented) Ulysses attention entries:
+// image outputs go to out_send ([world][seg_rows][h][D]) or, with out_blocks,
+// to one pointer per source segment (row stride out_row_stride).
+static int joint_common(const void* recv, const void* prefix_qkv, void* out_send, void* const* out_blocks,
+                        int64_t out_row_stride, void* prefix_out, int dtype, int out_dtype, int world, int seg_rows,
+                        int total, int prefix_len, const int* seg_valid, int heads_per_rank, int heads_valid,
+                        int head_dim, float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                        void* stream) {
+  if (world < 1 || seg_rows < 1 || total < 1 || prefix_len < 0 || heads_per_rank < 1 || heads_valid < 0 ||
+      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent joint Ulysses geometry");
+  if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
+  if (heads_valid == 0) return PS_B200_OK;
+  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows, P = prefix_len;
+  const int64_t block = n * h * D;
+  const char* base = static_cast<const char*>(recv);
+  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
+  int64_t out_st[4] = {int64_t(world) * block, block, h * D, D};
+  if (out_blocks) {
+    out_st[0] = out_st[1] = 0;
+    out_st[2] = out_row_stride;
+  }
+  SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  Prefix pre;
+  pre.len = prefix_len;
+  if (prefix_len) {
+    const char* pb = static_cast<const char*>(prefix_qkv);
+    const int64_t pblock = P * h * D;
+    const int64_t pst[4] = {3 * pblock, 3 * pblock, h * D, D};
+    pre.q = SegTensor{pb, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.k = SegTensor{pb + pblock * 2, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.v = SegTensor{pb + pblock * 4, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
+    pre.out = prefix_out;
+    pre.out_st[0] = pblock;
+    pre.out_st[1] = pblock;
+    pre.out_st[2] = h * D;
+    pre.out_st[3] = D;
+  }
+  return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
+                          world, total, seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status,
+                          stream, &pre, seg_valid, out_blocks);
+}
+
 extern "C" {
 
 int ps_b200_abi_version(void) { return PS_B200_ABI_VERSION; }
@@ -457,37 +502,38 @@ int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, voi
                                    const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
                                    float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
                                    void* stream) {
-  if (world < 1 || seg_rows < 1 || total < 1 || prefix_len < 0 || heads_per_rank < 1 || heads_valid < 0 ||
-      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
-    return set_error(PS_B200_ERR_INVALID, "inconsistent joint Ulysses geometry");
-  if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
-  if (heads_valid == 0) return PS_B200_OK;
-  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows, P = prefix_len;
-  const int64_t block = n * h * D;
-  const char* base = static_cast<const char*>(recv);
-  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
-  const int64_t out_st[4] = {int64_t(world) * block, block, h * D, D};
-  SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  Prefix pre;
-  pre.len = prefix_len;
-  if (prefix_len) {
-    const char* pb = static_cast<const char*>(prefix_qkv);
-    const int64_t pblock = P * h * D;
-    const int64_t pst[4] = {3 * pblock, 3 * pblock, h * D, D};
-    pre.q = SegTensor{pb, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
-    pre.k = SegTensor{pb + pblock * 2, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
-    pre.v = SegTensor{pb + pblock * 4, {pst[0], pst[1], pst[2], pst[3]}, heads_per_rank};
-    pre.out = prefix_out;
-    pre.out_st[0] = pblock;
-    pre.out_st[1] = pblock;
-    pre.out_st[2] = h * D;
-    pre.out_st[3] = D;
-  }
-  return attention_common(tq, tk, tv, out_send, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
-                          world, total, seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status,
-                          stream, &pre, seg_valid);
+  return joint_common(recv, prefix_qkv, out_send, nullptr, 0, prefix_out, dtype, out_dtype, world, seg_rows, total,
+                      prefix_len, seg_valid, heads_per_rank, heads_valid, head_dim, softmax_scale, workspace,
+                      workspace_bytes, status, stream);
+}
+
+int ps_b200_ulysses_joint_attn_to(const void* recv, const void* prefix_qkv, void* const* out_blocks,
+                                  int64_t out_row_stride, void* prefix_out, int dtype, int out_dtype, int world,
+                                  int seg_rows, int total, int prefix_len, const int* seg_valid, int heads_per_rank,
+                                  int heads_valid, int head_dim, float softmax_scale, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream) {
+  if (!out_blocks) return set_error(PS_B200_ERR_INVALID, "null output table");
+  if (out_row_stride < int64_t(heads_valid) * head_dim)
+    return set_error(PS_B200_ERR_INVALID, "output row stride below heads_valid * head_dim");
+  return joint_common(recv, prefix_qkv, nullptr, out_blocks, out_row_stride, prefix_out, dtype, out_dtype, world,
+                      seg_rows, total, prefix_len, seg_valid, heads_per_rank, heads_valid, head_dim, softmax_scale,
+                      workspace, workspace_bytes, status, stream);
+}
+
+int ps_b200_broadcast(void* const* dst, int ndst, const void* src, size_t bytes, void* stream) {
+  if (ndst < 1 || ndst > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "1..%d destinations", kMaxSegs);
+  if (bytes == 0) return PS_B200_OK;
+  if (!src || !dst || !aligned16(src) || bytes % 16 != 0)
+    return set_error(PS_B200_ERR_INVALID, "broadcast: 16-byte aligned source and a multiple of 16 bytes");
+  for (int d = 0; d < ndst; ++d)
+    if (!dst[d] || !aligned16(dst[d])) return set_error(PS_B200_ERR_INVALID, "broadcast destination %d", d);
+  if (int rc = check_device()) return rc;
+  BroadcastArgs a{};
+  a.src = src;
+  a.ndst = ndst;
+  for (int d = 0; d < ndst; ++d) a.dst[d] = dst[d];
+  a.vectors = static_cast<int64_t>(bytes / 16);
+  return launch_broadcast(a, static_cast<cudaStream_t>(stream));
 }
 
 int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtype, int out_dtype, int world,

@@ -89,6 +89,15 @@ struct UnpackArgs {
 
 int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream);
 
+struct BroadcastArgs {
+  const void* src;         // 16-byte vectors to copy
+  void* dst[kMaxSegs];     // destinations (this GPU's memory or a peer's)
+  int ndst;
+  int64_t vectors;
+};
+
+int launch_broadcast(const BroadcastArgs& a, cudaStream_t stream);
+
 // Error bookkeeping (thread-local message, returned code).
 int set_error(int code, const char* fmt, ...);
 int set_cuda_error(const char* what, cudaError_t err);

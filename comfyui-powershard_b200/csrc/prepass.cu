@@ -328,6 +328,16 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
   }
 }
 
+// Copies `vectors` 16-byte vectors of src to every destination: each vector
+// is read once and stored ndst times (grid-stride, coalesced).
+__global__ void __launch_bounds__(256) broadcast_kernel(const BroadcastArgs a) {
+  const uint4* src = static_cast<const uint4*>(a.src);
+  for (int64_t v = blockIdx.x * 256ll + threadIdx.x; v < a.vectors; v += static_cast<int64_t>(gridDim.x) * 256) {
+    const uint4 x = __ldg(src + v);
+    for (int d = 0; d < a.ndst; ++d) static_cast<uint4*>(a.dst[d])[v] = x;
+  }
+}
+
 }  // namespace pre
 
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
@@ -361,6 +371,20 @@ int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
   }
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return set_cuda_error("prepass launch", err);
+  count_launch();
+  return 0;
+}
+
+int launch_broadcast(const BroadcastArgs& a, cudaStream_t stream) {
+  using namespace pre;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (a.vectors + 255) / 256;
+  const int blocks = static_cast<int>(want < sms * 4LL ? want : sms * 4LL);
+  broadcast_kernel<<<blocks, 256, 0, stream>>>(a);
+  const cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return set_cuda_error("broadcast launch", err);
   count_launch();
   return 0;
 }

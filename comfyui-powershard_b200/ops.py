@@ -263,6 +263,47 @@ def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch
         status.arm()
 
 
+def ulysses_joint_attention_to(recv, prefix_qkv, out_blocks, out_row_stride: int, prefix_out,
+                               out_dtype: torch.dtype, geo: UlyssesGeometry, scale: float,
+                               status: DeviceStatus | None, workspace=None):
+    """``ulysses_joint_attention`` with the image outputs stored through one
+    device address per source segment (the owners' staging buffers)."""
+    lib = _lib.load()
+    _check16(recv, "joint attention recv")
+    _check16(prefix_qkv, "joint attention prefix")
+    if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
+        raise ValueError(f"joint attention: recv must be contiguous {geo.send_shape()}")
+    h, d = geo.heads_per_rank, geo.head_dim
+    if prefix_qkv.dim() != 4 or tuple(prefix_qkv.shape[::2]) != (3, h) or prefix_qkv.shape[3] != d \
+            or not prefix_qkv.is_contiguous() or prefix_qkv.dtype != recv.dtype:
+        raise ValueError(f"joint attention: prefix must be contiguous [3, P, {h}, {d}]")
+    plen = prefix_qkv.shape[1]
+    if tuple(prefix_out.shape) != (plen, h, d) or not prefix_out.is_contiguous() or prefix_out.dtype != out_dtype:
+        raise ValueError(f"joint attention: prefix out must be contiguous [{plen}, {h}, {d}] {out_dtype}")
+    if len(out_blocks) != geo.world:
+        raise ValueError(f"joint attention: {len(out_blocks)} output blocks for {geo.world} ranks")
+    rc = lib.ps_b200_ulysses_joint_attn_to(
+        recv.data_ptr(), prefix_qkv.data_ptr(), _lib.ptrs(out_blocks), int(out_row_stride), prefix_out.data_ptr(),
+        _lib.dtype_code(recv.dtype), _lib.dtype_code(out_dtype), geo.world, geo.width, geo.total, plen,
+        _seg_table(geo), h, geo.heads_valid, d, float(scale), *_ws(workspace),
+        status.ptr if status is not None else None, _lib.stream_handle(recv.device))
+    _lib.check(rc, "ps_b200_ulysses_joint_attn_to")
+    if status is not None:
+        status.arm()
+
+
+def broadcast(dst_ptrs, src: torch.Tensor):
+    """Copy the contiguous tensor ``src`` to every device address of
+    ``dst_ptrs`` (this GPU's memory or peers')."""
+    lib = _lib.load()
+    _lib.require_cuda(src, "broadcast")
+    if not src.is_contiguous():
+        raise ValueError("broadcast: source must be contiguous")
+    rc = lib.ps_b200_broadcast(_lib.ptrs(dst_ptrs), len(dst_ptrs), src.data_ptr(), src.numel() * src.element_size(),
+                               _lib.stream_handle(src.device))
+    _lib.check(rc, "ps_b200_broadcast")
+
+
 def unpack_staged(staging, out, geo: UlyssesGeometry):
     """Staging buffer [width, W*h, D] (rows of this rank, every head block) ->
     out [n_local, H, D] (real heads only)."""

@@ -9,7 +9,10 @@ into its address space (CUDA IPC):
   this rank at ``recv[s]`` directly over NVLink (``ps_b200_prepass_to``);
 * ``staging`` [width][W*h][D]: the attention kernel of rank r stores the
   output rows of this rank's tokens for heads [r*h, (r+1)*h) directly into
-  ``staging[:, r*h:(r+1)*h]`` (``ps_b200_ulysses_attn_to``).
+  ``staging[:, r*h:(r+1)*h]`` (``ps_b200_ulysses_attn_to``);
+* ``text`` [W][P][h][D] (joint attention only): rank r copies the text
+  outputs of its heads into ``text[r]`` of every rank (``ps_b200_broadcast``),
+  the all-gather over heads of the replicated text rows.
 
 So the transfers ride on the kernels' own stores and overlap their compute;
 what remains for the host is ordering across ranks.  ``barrier()`` is a
@@ -58,8 +61,9 @@ class PeerExchange:
     all-to-all.
     """
 
-    def __init__(self, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
+    def __init__(self, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
         self.group, self.geo, self.dtype, self.device = group, geo, dtype, device
+        self.text_rows = int(text_rows)
         self.own = []         # device pointers this rank allocated
         self.imported = []    # device pointers mapped from peers
         self.recv_ptrs = []
@@ -69,8 +73,8 @@ class PeerExchange:
 
     # ------------------------------------------------------------ setup
     @classmethod
-    def create(cls, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
-        ex = cls(group, geo, dtype, device)
+    def create(cls, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
+        ex = cls(group, geo, dtype, device, text_rows)
         ok, reason = ex._setup()
         verdict = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
         dist.all_reduce(verdict, op=dist.ReduceOp.MIN, group=group)
@@ -83,55 +87,58 @@ class PeerExchange:
         lib = _lib.load()
         geo = self.geo
         esize = torch.tensor([], dtype=self.dtype).element_size()
-        recv_shape = geo.send_shape()
-        stage_shape = (geo.width, geo.padded_heads, geo.head_dim)
+        h, d = geo.heads_per_rank, geo.head_dim
+        shapes = [geo.send_shape(), (geo.width, geo.padded_heads, d)]
+        if self.text_rows:
+            shapes.append((geo.world, self.text_rows, h, d))
+        nbytes = _lib.IPC_HANDLE_BYTES
         handles = bytearray()
         error = None
         try:
             with torch.cuda.device(self.device):
-                for shape in (recv_shape, stage_shape):
+                for shape in shapes:
                     ptr = ctypes.c_void_p()
                     _lib.check(lib.ps_b200_shared_alloc(max(1, math.prod(shape)) * esize, ctypes.byref(ptr)),
                                "ps_b200_shared_alloc")
                     self.own.append(ptr.value)
-                    h = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
-                    _lib.check(lib.ps_b200_ipc_export(ptr.value, h), "ps_b200_ipc_export")
-                    handles += bytes(h)
+                    hdl = (ctypes.c_ubyte * nbytes)()
+                    _lib.check(lib.ps_b200_ipc_export(ptr.value, hdl), "ps_b200_ipc_export")
+                    handles += bytes(hdl)
         except (RuntimeError, ValueError) as e:
             error = str(e)
-            handles = bytearray(2 * _lib.IPC_HANDLE_BYTES)
+            handles = bytearray(len(shapes) * nbytes)
         table = [None] * geo.world
         dist.all_gather_object(table, (socket.gethostname(), bytes(handles), error), group=self.group)
         if any(entry[2] for entry in table):
             return False, next(entry[2] for entry in table if entry[2])
         if len({entry[0] for entry in table}) != 1:
             return False, "ranks on more than one host"
+        ptrs = [[] for _ in shapes]  # ptrs[buffer][rank]
         try:
             with torch.cuda.device(self.device):
                 for r, (_, blob, _) in enumerate(table):
-                    if r == geo.rank:
-                        self.recv_ptrs.append(self.own[0])
-                        self.stage_ptrs.append(self.own[1])
-                        continue
-                    mapped = []
-                    for part in range(2):
-                        h = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES).from_buffer_copy(
-                            blob[part * _lib.IPC_HANDLE_BYTES:(part + 1) * _lib.IPC_HANDLE_BYTES])
+                    for part in range(len(shapes)):
+                        if r == geo.rank:
+                            ptrs[part].append(self.own[part])
+                            continue
+                        hdl = (ctypes.c_ubyte * nbytes).from_buffer_copy(blob[part * nbytes:(part + 1) * nbytes])
                         ptr = ctypes.c_void_p()
-                        _lib.check(lib.ps_b200_ipc_import(h, ctypes.byref(ptr)), "ps_b200_ipc_import")
+                        _lib.check(lib.ps_b200_ipc_import(hdl, ctypes.byref(ptr)), "ps_b200_ipc_import")
                         self.imported.append(ptr.value)
-                        mapped.append(ptr.value)
-                    self.recv_ptrs.append(mapped[0])
-                    self.stage_ptrs.append(mapped[1])
+                        ptrs[part].append(ptr.value)
         except (RuntimeError, ValueError) as e:
             return False, str(e)
-        self.recv = _wrap(self.own[0], recv_shape, self.dtype, self.device)
-        self.staging = _wrap(self.own[1], stage_shape, self.dtype, self.device)
-        h, d = geo.heads_per_rank, geo.head_dim
+        self.recv_ptrs, self.stage_ptrs = ptrs[0], ptrs[1]
+        self.recv = _wrap(self.own[0], shapes[0], self.dtype, self.device)
+        self.staging = _wrap(self.own[1], shapes[1], self.dtype, self.device)
         block = 3 * geo.width * h * d * esize                   # one source's [3][width][h][D] block
         self.dst_blocks = [p + geo.rank * block for p in self.recv_ptrs]
         self.out_blocks = [p + geo.rank * h * d * esize for p in self.stage_ptrs]
         self.out_row_stride = geo.padded_heads * d
+        if self.text_rows:
+            self.text = _wrap(self.own[2], shapes[2], self.dtype, self.device)
+            tblock = self.text_rows * h * d * esize
+            self.text_dst = [p + geo.rank * tblock for p in ptrs[2]]
         return True, None
 
     # ------------------------------------------------------------ per step

@@ -94,17 +94,18 @@ class UlyssesAttention:
         if geo.world > 1:
             dist.all_to_all_single(recv, send, group=self.group)
 
-    def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
+    def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
         """The peer exchange of this geometry, or None for the NCCL path."""
         if geo.world == 1 or self.exchange == "nccl" or self.kernels is not ops or device.type != "cuda":
             return None
         if self.exchange == "auto" and dist.get_backend(self.group) != "nccl":
             return None
         stream = torch.cuda.current_stream(device).cuda_stream
-        key = (device.index, stream, geo.world, geo.rank, geo.width, geo.heads_per_rank, geo.head_dim, dtype)
+        key = (device.index, stream, geo.world, geo.rank, geo.width, geo.heads_per_rank, geo.head_dim, dtype,
+               text_rows)
         if key not in self._peers:
             from .peer import PeerExchange
-            ex = PeerExchange.create(self.group, geo, dtype, device)
+            ex = PeerExchange.create(self.group, geo, dtype, device, text_rows)
             if ex is None and self.exchange == "peer":
                 raise RuntimeError("peer exchange requested but the ranks cannot map each other's memory")
             self._peers[key] = ex
@@ -314,6 +315,24 @@ class UlyssesAttention:
             else:
                 img_out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
                 txt_out = torch.empty((plen, heads, head_dim), dtype=out_dtype, device=device)
+            px = self._peer(geo, dtype, device, text_rows=plen)
+            if px is not None:
+                # Image rows cross by peer stores, the text outputs of this
+                # rank's heads are copied into every rank's text buffer.
+                if plen:
+                    k.prepass(*txt, w_q, w_k, txt_freqs, tb["send"], tgeo, eps, norm)
+                k.prepass_to(*img, w_q, w_k, img_freqs, px.dst_blocks, geo, dtype, eps, norm)
+                px.barrier()
+                k.ulysses_joint_attention_to(px.recv, tb["send"][geo.rank], px.out_blocks, px.out_row_stride,
+                                             tb["out"], dtype, geo, scale, status, **self._ws(device))
+                if plen:
+                    k.broadcast(px.text_dst, tb["out"])
+                px.barrier()
+                k.unpack_staged(px.staging, img_out, geo)
+                if plen:
+                    k.unpack(px.text.view(tgeo.out_shape()), txt_out, tgeo)
+                self._count_joint(state, geo, dtype, "peer")
+                return txt_out, img_out
             if plen:
                 k.prepass(*txt, w_q, w_k, txt_freqs, tb["send"], tgeo, eps, norm)
             k.prepass(*img, w_q, w_k, img_freqs, ws["send"], geo, eps, norm)
@@ -330,14 +349,20 @@ class UlyssesAttention:
                 if plen:
                     dist.all_gather_into_tensor(tb["gathered"], tb["out"], group=self.group)
                     k.unpack(tb["gathered"].view(tgeo.out_shape()), txt_out, tgeo)
-        if state is not None:
-            qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
-            state["padded_heads"] = geo.padded_heads
-            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
-            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
-            state["out_collectives"] = state.get("out_collectives", 0) + 2
-            state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
+        self._count_joint(state, geo, dtype, "nccl" if geo.world > 1 else "local")
         return txt_out, img_out
+
+    @staticmethod
+    def _count_joint(state, geo, dtype, exchange):
+        if state is None:
+            return
+        qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+        state["padded_heads"] = geo.padded_heads
+        state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+        state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
+        state["out_collectives"] = state.get("out_collectives", 0) + 2
+        state["out_exchanged_bytes"] = state.get("out_exchanged_bytes", 0) + out_bytes
+        state["exchange"] = exchange
 
     def check(self):
         """Synchronize and raise if any attention launch aborted on the device."""

@@ -237,6 +237,25 @@ int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const 
                        int norm_rope, int rope_style, int rope_pairs, void* stream);
 
 /*
+ * Joint attention (as ps_b200_ulysses_joint_attn_fwd) with the image outputs
+ * stored through one pointer per source segment (row stride out_row_stride
+ * elements, head j at + j*head_dim): the peer exchange's staging buffers.
+ * Text outputs go to prefix_out as there.
+ */
+int ps_b200_ulysses_joint_attn_to(const void* recv, const void* prefix_qkv, void* const* out_blocks,
+                                  int64_t out_row_stride, void* prefix_out, int dtype, int out_dtype, int world,
+                                  int seg_rows, int total, int prefix_len, const int* seg_valid, int heads_per_rank,
+                                  int heads_valid, int head_dim, float softmax_scale, void* workspace,
+                                  size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * Copies `bytes` (a multiple of 16, 16-byte aligned) from src to each of the
+ * ndst (1..64) destinations, which may be other GPUs' memory: the all-gather
+ * of the text outputs in the peer exchange of joint attention.
+ */
+int ps_b200_broadcast(void* const* dst, int ndst, const void* src, size_t bytes, void* stream);
+
+/*
  * ps_b200_ulysses_attn_fwd with one output pointer per source segment: valid
  * row i of segment s, head j goes to out_blocks[s] + i*out_row_stride +
  * j*head_dim elements (out_dtype), possibly another GPU's memory.
