@@ -86,7 +86,7 @@ class PeerExchange:
     def _setup(self):
         lib = _lib.load()
         geo = self.geo
-        esize = torch.tensor([], dtype=self.dtype).element_size()
+        esize = self.dtype.itemsize
         h, d = geo.heads_per_rank, geo.head_dim
         shapes = [geo.send_shape(), (geo.width, geo.padded_heads, d)]
         if self.text_rows:

@@ -198,7 +198,7 @@ class UlyssesAttention:
         one q/k/v exchange and one output exchange per block, with their bytes."""
         if state is None:
             return
-        qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+        qkv_bytes, out_bytes = geo.exchanged_bytes(dtype.itemsize)
         state["padded_heads"] = geo.padded_heads
         state["kv_collectives"] = state.get("kv_collectives", 0) + 1
         state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
@@ -256,7 +256,7 @@ class UlyssesAttention:
             out = torch.empty((n, heads, head_dim), dtype=out_dtype, device=device)
             k.token_attention(tb["qkv"], kv, out, n, total, scale, status, **self._ws(device))
         if state is not None:
-            esize = torch.tensor([], dtype=dtype).element_size()
+            esize = dtype.itemsize
             state["kv_collectives"] = state.get("kv_collectives", 0) + 1
             state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + 2 * total * heads * head_dim * esize
             state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
@@ -356,7 +356,7 @@ class UlyssesAttention:
     def _count_joint(state, geo, dtype, exchange):
         if state is None:
             return
-        qkv_bytes, out_bytes = geo.exchanged_bytes(torch.tensor([], dtype=dtype).element_size())
+        qkv_bytes, out_bytes = geo.exchanged_bytes(dtype.itemsize)
         state["padded_heads"] = geo.padded_heads
         state["kv_collectives"] = state.get("kv_collectives", 0) + 1
         state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes

@@ -35,6 +35,17 @@
  *                          of wan_model.py:360 and :376 replaced by peer
  *                          stores (no reference counterpart for the buffer
  *                          sharing itself: NCCL owns it there).
+ *   ps_b200_ulysses_joint_attn_fwd, ps_b200_ulysses_joint_attn_to,
+ *   ps_b200_broadcast       the attention of image_parallel.SequenceAttention
+ *                          (powershard/image_parallel.py:96-110: replicated
+ *                          text rows + split image rows), computed on the
+ *                          Ulysses exchange instead of the reference's K/V
+ *                          all-gather; the broadcast all-gathers text outputs.
+ *   ps_b200_prepass rope_style 1   rope_split_half of the H3 path,
+ *                          powershard/attention.py:98-103.
+ *   ps_b200_kernel_launches, ps_b200_selftest_bounded_wait,
+ *   ps_b200_block_fwd_static  no reference counterpart (instrumentation,
+ *                          failure-detection self-test, allocation-free block).
  *
  * Layout vocabulary: a "segmented" tensor is [batch][segment][row][head][d]
  * with arbitrary element strides for the first four axes and d contiguous.
