@@ -646,11 +646,19 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs args) 
 }  // namespace attn
 
 namespace {
+// Raises the kernel's dynamic shared memory limit once per device (outside
+// any stream capture that may follow: the first launch on a device does it).
 template <bool kFp16>
 int prepare_kernel() {
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (done[dev]) return 0;
   const cudaError_t err = cudaFuncSetAttribute(attn::attn_fwd_kernel<kFp16>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, attn::kSmemBytes);
-  return err == cudaSuccess ? 0 : set_cuda_error("attention: cudaFuncSetAttribute", err);
+  if (err != cudaSuccess) return set_cuda_error("attention: cudaFuncSetAttribute", err);
+  done[dev] = true;
+  return 0;
 }
 }  // namespace
 

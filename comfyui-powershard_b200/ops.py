@@ -19,6 +19,8 @@ class DeviceStatus:
     its bounded internal waits expires.  ``arm()`` queues a 4-byte copy of the
     word to pinned host memory after a launch; ``poll()`` (cheap, no sync)
     raises if a completed copy shows an error; ``check()`` synchronizes.
+    While a CUDA graph is being captured, ``arm`` and ``poll`` do nothing
+    (the kernels still write the word; ``check()`` after a replay reads it).
     """
 
     def __init__(self, device: torch.device):
@@ -32,11 +34,15 @@ class DeviceStatus:
         return self.word.data_ptr()
 
     def arm(self):
+        if torch.cuda.is_current_stream_capturing():
+            return
         self.host.copy_(self.word, non_blocking=True)
         self.event = torch.cuda.Event()
         self.event.record(torch.cuda.current_stream(self.device))
 
     def poll(self):
+        if torch.cuda.is_current_stream_capturing():
+            return
         if self.event is not None and self.event.query():
             self._raise_if_set(int(self.host.item()))
 
