@@ -281,7 +281,8 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
                    const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
                    const float* freqs, int64_t freqs_row_stride, void* const* dst, int dtype,
                    int world, int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
-                   int norm_rope, int rope_style, int rope_pairs, void* stream) {
+                   int norm_rope, int rope_style, int rope_pairs, void* stream, void* q_out = nullptr,
+                   int kv_fanout = 0) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
   if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
       int64_t(heads_per_rank) * world < heads || head_dim <= 0)
@@ -334,7 +335,9 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
   a.w_fp32 = w_dtype == PS_B200_FP32;
   a.freqs = freqs;
   a.freqs_row_stride = freqs_row_stride;
-  for (int d = 0; d < world; ++d) a.dst[d] = dst[d];
+  for (int d = 0; d < (kv_fanout > world ? kv_fanout : world); ++d) a.dst[d] = dst[d];
+  a.q_out = q_out;
+  a.kv_fanout = kv_fanout;
   a.world = world;
   a.n_local = n_local;
   a.seg_rows = seg_rows;
@@ -448,6 +451,24 @@ int ps_b200_attn_fwd(const void* q, const int64_t q_strides[4], const void* k, c
   return attention_common(tq, tk, tv, out, out_strides, dtype, out_dtype, batch, heads_q, heads_q / heads_kv, head_dim,
                           seg_rows_q, segs_q, len_q, seg_rows_k, segs_k, len_k, softmax_scale, workspace,
                           workspace_bytes, status, stream);
+}
+
+int ps_b200_prepass_token_to(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                             const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                             const float* freqs, int64_t freqs_row_stride, void* q_out, void* const* kv_dst,
+                             int ndst, int dtype, int n_local, int width, int heads, int head_dim, float eps,
+                             int norm_rope, int rope_style, int rope_pairs, void* stream) {
+  if (ndst < 1 || ndst > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "1..%d k/v destinations", kMaxSegs);
+  if (width > 0) {
+    if (!q_out || !aligned16(q_out)) return set_error(PS_B200_ERR_INVALID, "q output null or not 16-byte aligned");
+    if (!kv_dst) return set_error(PS_B200_ERR_INVALID, "null k/v destination table");
+    for (int d = 0; d < ndst; ++d)
+      if (!kv_dst[d] || !aligned16(kv_dst[d]))
+        return set_error(PS_B200_ERR_INVALID, "k/v destination %d null or not 16-byte aligned", d);
+  }
+  return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
+                        freqs_row_stride, kv_dst, dtype, 1, n_local, width, heads, heads, head_dim, eps, norm_rope,
+                        rope_style, rope_pairs, stream, q_out, ndst);
 }
 
 int ps_b200_ulysses_attn_fwd(const void* recv, void* out_send, int dtype, int out_dtype, int world, int seg_rows,

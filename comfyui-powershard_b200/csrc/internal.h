@@ -74,6 +74,11 @@ struct PrepassArgs {
   int norm_rope;           // 0: plain pack, 1: full-width RMSNorm + RoPE, 2: per-head RMSNorm + RoPE
   int rope_style;          // 0: interleaved pairs (2j, 2j+1) over the head; 1: split half (j, j+rope_pairs)
   int rope_pairs;          // rotated pairs per head (head_dim/2 for style 0; a multiple of 8 for style 1)
+  // Token-mode fan-out (kv_fanout > 0, world 1, heads_per_rank == heads): q rows go to q_out
+  // [seg_rows][heads][head_dim]; k and v rows go to each of dst[0..kv_fanout-1], blocks
+  // [2][seg_rows][heads][head_dim] (the all-gather of K/V as stores).
+  void* q_out;
+  int kv_fanout;
 };
 
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);

@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
   __shared__ uint16_t* sdst[kMaxSegs];
   const int i = blockIdx.x;
   const int tid = threadIdx.x;
-  if (tid < a.world) sdst[tid] = static_cast<uint16_t*>(a.dst[tid]);
+  if (tid < (a.kv_fanout > a.world ? a.kv_fanout : a.world)) sdst[tid] = static_cast<uint16_t*>(a.dst[tid]);
   __syncthreads();
   const int D = a.head_dim;
   const int h = a.heads_per_rank;
@@ -109,13 +109,27 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
     return sdst[dst] + row_off + static_cast<int64_t>(j) * D + dd;
   };
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  // Store one 16-byte vector of `kind` (0 q, 1 k, 2 v) for head g, element dd.
+  auto put = [&](int kind, int g, int dd, const uint4& val) {
+    if (a.kv_fanout) {
+      const int64_t off = row_off + static_cast<int64_t>(g) * D + dd;
+      if (kind == 0) {
+        *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.q_out) + off) = val;
+      } else {
+        for (int d = 0; d < a.kv_fanout; ++d)
+          *reinterpret_cast<uint4*>(sdst[d] + (kind - 1) * block_elems + off) = val;
+      }
+    } else {
+      *reinterpret_cast<uint4*>(slot0(g, dd) + kind * block_elems) = val;
+    }
+  };
 
   if (i >= a.n_local) {  // token padding of the last ranks: zeros for every head
     const int total = a.world * h * vph;
     for (int kind = 0; kind < 3; ++kind)
       for (int v = tid; v < total; v += kThreads) {
         const int g = v / vph;
-        *reinterpret_cast<uint4*>(slot0(g, (v - g * vph) * 8) + kind * block_elems) = zero;
+        put(kind, g, (v - g * vph) * 8, zero);
       }
     return;
   }
@@ -139,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
   }
 #pragma unroll
   for (int u = 0; u < kVec; ++u)
-    if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], ddv[u]) + 2 * block_elems) = xv[2][u];
+    if (live[u]) put(2, gv[u], ddv[u], xv[2][u]);
 
   if (a.norm_rope) {
     const bool per_head = a.norm_rope == 2;  // Flux QK-norm: statistic per head, weight [head_dim]
@@ -277,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
             }
           }
         }
-        if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], dd) + kind * block_elems) = pack8(o);
+        if (live[u]) put(kind, gv[u], dd, pack8(o));
       }
     }
   } else {
@@ -285,14 +299,14 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
     for (int kind = 0; kind < 2; ++kind)
 #pragma unroll
       for (int u = 0; u < kVec; ++u)
-        if (live[u]) *reinterpret_cast<uint4*>(slot0(gv[u], ddv[u]) + kind * block_elems) = xv[kind][u];
+        if (live[u]) put(kind, gv[u], ddv[u], xv[kind][u]);
   }
   // Head padding: slots of heads [heads, world*h) are zero.
   const int padded = (a.world * h - a.heads) * vph;
   for (int kind = 0; kind < 3; ++kind)
     for (int v = tid; v < padded; v += kThreads) {
       const int g = a.heads + v / vph;
-      *reinterpret_cast<uint4*>(slot0(g, (v % vph) * 8) + kind * block_elems) = zero;
+      put(kind, g, (v % vph) * 8, zero);
     }
 }
 

@@ -349,20 +349,44 @@ def token_pack(x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local: int, heads: int, he
     _lib.check(rc, "ps_b200_prepass (token mode)")
 
 
-def token_attention(qkv, kv_all, out, n_local: int, total: int, scale: float, status: DeviceStatus | None,
-                    workspace=None):
-    """Token mode, step 3: this rank's queries qkv[0] (first n_local rows)
-    against the gathered keys/values kv_all [W, 2, width, H, D] (segment s
-    holds rank s's shard_bounds rows) -> out [n_local, H, D] directly."""
+def token_pack_to(x_q, x_k, x_v, w_q, w_k, freqs, q_out, kv_dst, n_local: int, heads: int, head_dim: int,
+                  eps: float = 1e-6, norm_rope=True, rope_split_pairs=None):
+    """Token mode with the K/V all-gather as stores: q of this rank's rows to
+    ``q_out`` [width, H, D], k/v to the [2, width, H, D] block at each device
+    address of ``kv_dst`` (every rank's gathered K/V, this rank's slot)."""
+    mode = int(norm_rope)
     lib = _lib.load()
-    _check16(qkv, "token attention q")
+    _check16(q_out, "token pack q")
+    width = q_out.shape[0]
+    if q_out.dim() != 3 or tuple(q_out.shape[1:]) != (heads, head_dim) or not q_out.is_contiguous():
+        raise ValueError(f"token pack: q_out must be contiguous [width, {heads}, {head_dim}]")
+    geo = UlyssesGeometry(total=n_local, heads=heads, head_dim=head_dim, world=1, rank=0)
+    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, q_out.dtype, q_out.device, mode, rope_split_pairs)
+    rc = lib.ps_b200_prepass_token_to(
+        *args, q_out.data_ptr(), _lib.ptrs(kv_dst), len(kv_dst), _lib.dtype_code(q_out.dtype), n_local, width,
+        heads, head_dim, float(eps), mode, *_rope_args(head_dim, rope_split_pairs), _lib.stream_handle(q_out.device))
+    _lib.check(rc, "ps_b200_prepass_token_to")
+
+
+def token_attention(q, kv_all, out, n_local: int, total: int, scale: float, status: DeviceStatus | None,
+                    workspace=None):
+    """Token mode, step 3: this rank's queries q [width, H, D] (first n_local
+    rows; a [3, width, H, D] block is read as its q part) against the gathered
+    keys/values kv_all [W, 2, width, H, D] (segment s holds rank s's
+    shard_bounds rows) -> out [n_local, H, D] directly."""
+    lib = _lib.load()
+    if q.dim() == 4:
+        q = q[0]
+    _check16(q, "token attention q")
     _check16(kv_all, "token attention kv")
     _lib.require_cuda(out, "token attention out")
-    _, width, heads, d = qkv.shape
+    if not q.is_contiguous():
+        raise ValueError("token attention: q must be contiguous")
+    width, heads, d = q.shape
     world = kv_all.shape[0]
     if tuple(kv_all.shape) != (world, 2, width, heads, d) or not kv_all.is_contiguous():
         raise ValueError(f"token attention: kv_all must be contiguous [W, 2, {width}, {heads}, {d}]")
-    if tuple(out.shape) != (n_local, heads, d) or not out.is_contiguous() or out.dtype not in (qkv.dtype,
+    if tuple(out.shape) != (n_local, heads, d) or not out.is_contiguous() or out.dtype not in (q.dtype,
                                                                                             torch.float32):
         raise ValueError(f"token attention: out must be contiguous [{n_local}, {heads}, {d}]")
     row, seg = heads * d, 2 * width * heads * d
@@ -371,10 +395,10 @@ def token_attention(qkv, kv_all, out, n_local: int, total: int, scale: float, st
     o_st = _lib.i64([0, 0, row, d])
     esize = kv_all.element_size()
     rc = lib.ps_b200_attn_fwd(
-        qkv.data_ptr(), q_st, kv_all.data_ptr(), kv_st, kv_all.data_ptr() + width * row * esize, kv_st,
-        out.data_ptr(), o_st, _lib.dtype_code(qkv.dtype), _lib.dtype_code(out.dtype), 1, heads, heads, d,
+        q.data_ptr(), q_st, kv_all.data_ptr(), kv_st, kv_all.data_ptr() + width * row * esize, kv_st,
+        out.data_ptr(), o_st, _lib.dtype_code(q.dtype), _lib.dtype_code(out.dtype), 1, heads, heads, d,
         width, 1, n_local, width, world, total, float(scale), *_ws(workspace),
-        status.ptr if status is not None else None, _lib.stream_handle(qkv.device))
+        status.ptr if status is not None else None, _lib.stream_handle(q.device))
     _lib.check(rc, "ps_b200_attn_fwd (token mode)")
     if status is not None:
         status.arm()

@@ -12,7 +12,10 @@ into its address space (CUDA IPC):
   ``staging[:, r*h:(r+1)*h]`` (``ps_b200_ulysses_attn_to``);
 * ``text`` [W][P][h][D] (joint attention only): rank r copies the text
   outputs of its heads into ``text[r]`` of every rank (``ps_b200_broadcast``),
-  the all-gather over heads of the replicated text rows.
+  the all-gather over heads of the replicated text rows;
+* token layout: one buffer ``kv_all`` [W][2][width][H][D]; rank r's
+  pre-pass stores its k/v rows into slot r of every rank's buffer
+  (``ps_b200_prepass_token_to``), the K/V all-gather of token mode.
 
 So the transfers ride on the kernels' own stores and overlap their compute;
 what remains for the host is ordering across ranks.  ``barrier()`` is a
@@ -61,9 +64,11 @@ class PeerExchange:
     all-to-all.
     """
 
-    def __init__(self, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
+    def __init__(self, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
+                 layout: str = "ulysses"):
         self.group, self.geo, self.dtype, self.device = group, geo, dtype, device
         self.text_rows = int(text_rows)
+        self.layout = layout
         self.own = []         # device pointers this rank allocated
         self.imported = []    # device pointers mapped from peers
         self.recv_ptrs = []
@@ -73,8 +78,9 @@ class PeerExchange:
 
     # ------------------------------------------------------------ setup
     @classmethod
-    def create(cls, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
-        ex = cls(group, geo, dtype, device, text_rows)
+    def create(cls, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
+               layout: str = "ulysses"):
+        ex = cls(group, geo, dtype, device, text_rows, layout)
         ok, reason = ex._setup()
         verdict = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
         dist.all_reduce(verdict, op=dist.ReduceOp.MIN, group=group)
@@ -88,9 +94,12 @@ class PeerExchange:
         geo = self.geo
         esize = self.dtype.itemsize
         h, d = geo.heads_per_rank, geo.head_dim
-        shapes = [geo.send_shape(), (geo.width, geo.padded_heads, d)]
-        if self.text_rows:
-            shapes.append((geo.world, self.text_rows, h, d))
+        if self.layout == "token":  # gathered K/V of every rank: [W][2][width][H][D]
+            shapes = [(geo.world, 2, geo.width, geo.heads, d)]
+        else:
+            shapes = [geo.send_shape(), (geo.width, geo.padded_heads, d)]
+            if self.text_rows:
+                shapes.append((geo.world, self.text_rows, h, d))
         nbytes = _lib.IPC_HANDLE_BYTES
         handles = bytearray()
         error = None
@@ -128,6 +137,11 @@ class PeerExchange:
                         ptrs[part].append(ptr.value)
         except (RuntimeError, ValueError) as e:
             return False, str(e)
+        if self.layout == "token":
+            self.kv_all = _wrap(self.own[0], shapes[0], self.dtype, self.device)
+            kv_block = 2 * geo.width * geo.heads * d * esize     # one rank's [2][width][H][D] slot
+            self.kv_dst = [p + geo.rank * kv_block for p in ptrs[0]]
+            return True, None
         self.recv_ptrs, self.stage_ptrs = ptrs[0], ptrs[1]
         self.recv = _wrap(self.own[0], shapes[0], self.dtype, self.device)
         self.staging = _wrap(self.own[1], shapes[1], self.dtype, self.device)

@@ -94,18 +94,19 @@ class UlyssesAttention:
         if geo.world > 1:
             dist.all_to_all_single(recv, send, group=self.group)
 
-    def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0):
+    def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
+              layout: str = "ulysses"):
         """The peer exchange of this geometry, or None for the NCCL path."""
         if geo.world == 1 or self.exchange == "nccl" or self.kernels is not ops or device.type != "cuda":
             return None
         if self.exchange == "auto" and dist.get_backend(self.group) != "nccl":
             return None
         stream = torch.cuda.current_stream(device).cuda_stream
-        key = (device.index, stream, geo.world, geo.rank, geo.width, geo.heads_per_rank, geo.head_dim, dtype,
+        key = (layout, device.index, stream, geo.world, geo.rank, geo.width, geo.heads, geo.head_dim, dtype,
                text_rows)
         if key not in self._peers:
             from .peer import PeerExchange
-            ex = PeerExchange.create(self.group, geo, dtype, device, text_rows)
+            ex = PeerExchange.create(self.group, geo, dtype, device, text_rows, layout)
             if ex is None and self.exchange == "peer":
                 raise RuntimeError("peer exchange requested but the ranks cannot map each other's memory")
             self._peers[key] = ex
@@ -220,7 +221,9 @@ class UlyssesAttention:
         [3, width, H, D]; all-gather of its k/v part into [W, 2, width, H, D]
         (the rows of gather_tokens, wan_model.py:336-340 / attention.py:40-54,
         padded to equal width); attention of the local queries against the W
-        key segments, written straight to the [n, H, D] output.
+        key segments, written straight to the [n, H, D] output.  With the
+        peer exchange the pre-pass stores the k/v rows straight into every
+        rank's gathered buffer instead (two 4-byte all-reduces order it).
         """
         device = x_q.device
         dtype = x_q.dtype
@@ -238,6 +241,23 @@ class UlyssesAttention:
             status = self._device_status(device)
             status.poll()
             stream = torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else 0
+            if world > 1:
+                geo = UlyssesGeometry(total=total, heads=heads, head_dim=head_dim, world=world, rank=rank)
+                px = self._peer(geo, dtype, device, layout="token")
+                if px is not None:
+                    # k/v rows stored straight into every rank's gathered buffer.
+                    qkey = ("token_q", device.index, stream, width, heads, head_dim, dtype)
+                    if qkey not in self._buffers:
+                        self._buffers[qkey] = torch.empty((width, heads, head_dim), dtype=dtype, device=device)
+                    q_loc = self._buffers[qkey]
+                    k.token_pack_to(x_q, x_k, x_v, w_q, w_k, freqs, q_loc, px.kv_dst, n, heads, head_dim, eps,
+                                    norm_rope, **self._rope_kw(rope_split_pairs))
+                    px.barrier()
+                    out = torch.empty((n, heads, head_dim), dtype=out_dtype, device=device)
+                    k.token_attention(q_loc, px.kv_all, out, n, total, scale, status, **self._ws(device))
+                    px.barrier()
+                    self._count_token(state, total, heads, head_dim, dtype, "peer")
+                    return out
             key = ("token", device.index, stream, world, width, heads, head_dim, dtype)
             tb = self._buffers.get(key)
             if tb is None:
@@ -255,13 +275,18 @@ class UlyssesAttention:
                 kv = tb["qkv"][1:].unsqueeze(0)  # one segment: this rank's own rows
             out = torch.empty((n, heads, head_dim), dtype=out_dtype, device=device)
             k.token_attention(tb["qkv"], kv, out, n, total, scale, status, **self._ws(device))
-        if state is not None:
-            esize = dtype.itemsize
-            state["kv_collectives"] = state.get("kv_collectives", 0) + 1
-            state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + 2 * total * heads * head_dim * esize
-            state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
-            state["exchange"] = "nccl" if world > 1 else "local"
+        self._count_token(state, total, heads, head_dim, dtype, "nccl" if world > 1 else "local")
         return out
+
+    @staticmethod
+    def _count_token(state, total, heads, head_dim, dtype, exchange):
+        """Token-mode counters (wan_model.py:489-500): one K/V gather per block."""
+        if state is None:
+            return
+        state["kv_collectives"] = state.get("kv_collectives", 0) + 1
+        state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + 2 * total * heads * head_dim * dtype.itemsize
+        state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
+        state["exchange"] = exchange
 
     def forward_joint(self, txt, img, w_q=None, w_k=None, txt_freqs=None, img_freqs=None, *, total_img: int,
                       heads: int, eps: float = 1e-6, scale: float | None = None,

@@ -248,6 +248,20 @@ int ps_b200_prepass_to(const void* x_q, const void* x_k, const void* x_v, const 
                        int norm_rope, int rope_style, int rope_pairs, void* stream);
 
 /*
+ * Token mode with the K/V all-gather as stores: the pre-pass of this rank's
+ * n_local rows (as ps_b200_prepass, world 1, all heads) writes q to q_out
+ * [width][heads][head_dim] and k, v to each of the ndst (1..64) blocks
+ * kv_dst[d], [2][width][heads][head_dim] (rank d's gathered K/V, slot of
+ * this rank; possibly another GPU's memory).  Rows n_local..width-1 are
+ * zeros.  Replaces the pack + gather_tokens of wan_model.py:489-500.
+ */
+int ps_b200_prepass_token_to(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
+                             const int64_t x_head_strides[3], const void* w_qnorm, const void* w_knorm, int w_dtype,
+                             const float* freqs, int64_t freqs_row_stride, void* q_out, void* const* kv_dst,
+                             int ndst, int dtype, int n_local, int width, int heads, int head_dim, float eps,
+                             int norm_rope, int rope_style, int rope_pairs, void* stream);
+
+/*
  * Joint attention (as ps_b200_ulysses_joint_attn_fwd) with the image outputs
  * stored through one pointer per source segment (row stride out_row_stride
  * elements, head j at + j*head_dim): the peer exchange's staging buffers.

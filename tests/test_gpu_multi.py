@@ -42,15 +42,16 @@ def nccl_worker(rank, world, port, report, total, heads, exchange):
         wk = torch.rand(heads * 128, generator=g) + 0.5
         freqs = oracle.rope_table_3d((total // 100 + 1, 10, 10), 128)[:, :total]
         a, b = oracle.shard_bounds(total, rank, world)
-        engine = UlyssesAttention(exchange="nccl" if exchange == "token" else exchange)
-        run = engine.forward_token if exchange == "token" else engine.forward
+        token = exchange.startswith("token")
+        engine = UlyssesAttention(exchange={"token": "nccl", "token_peer": "peer"}.get(exchange, exchange))
+        run = engine.forward_token if token else engine.forward
         state = {}
         outs = []
         for _ in range(2):
             outs.append(run(*(t[0, a:b].to(dev) for t in x), wq.to(dev), wk.to(dev),
                             freqs[0, a:b, 0].to(dev), total=total, heads=heads, state=state))
         engine.check()
-        if exchange == "token":
+        if token:
             expected = oracle.token_sequence_attention(*(t.float() for t in x), wq, wk, freqs, heads,
                                                        world)[rank][0].float()
         else:
@@ -61,7 +62,7 @@ def nccl_worker(rank, world, port, report, total, heads, exchange):
             rel = float(err.mean() / expected.abs().mean()) if expected.numel() else 0.0
             errs.append((float(err.max()) if err.numel() else 0.0, rel))
         ok = all(e <= 2e-2 and r <= 5e-3 for e, r in errs) and state["kv_collectives"] == 2
-        ok = ok and state["exchange"] == ("nccl" if exchange == "token" else exchange)
+        ok = ok and state["exchange"] == {"token": "nccl", "token_peer": "peer"}.get(exchange, exchange)
         ok = ok and torch.equal(outs[0], outs[1])
         engine.close()
         Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank,
@@ -70,7 +71,7 @@ def nccl_worker(rank, world, port, report, total, heads, exchange):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer", "token"])
+@pytest.mark.parametrize("exchange", ["nccl", "peer", "token", "token_peer"])
 @pytest.mark.parametrize("world,total,heads", [(2, 1000, 40), (2, 37, 5), (4, 1023, 40), (8, 4099, 40),
                                                (3, 300, 24)])
 def test_engine_over_nccl(world, total, heads, exchange, tmp_path, cuda_lib):
