@@ -1,9 +1,8 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run once in a container that has the ComfyUI-PowerShard source tree
-(default ``/root/reference``; override with POWERSHARD_REFERENCE):
+Run once where a ComfyUI-PowerShard source tree is available, naming it:
 
-    python tests/golden/make_golden.py
+    POWERSHARD_REFERENCE=<path to the ComfyUI-PowerShard tree> python tests/golden/make_golden.py
 
 It imports the reference package from that tree (torch only, no ComfyUI),
 runs the reference's own hot-path functions on seeded inputs and saves
@@ -43,7 +42,7 @@ import torch
 import torch.distributed as dist
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("POWERSHARD_REFERENCE", "/root/reference"))
+REF = Path(os.environ["POWERSHARD_REFERENCE"]) if "POWERSHARD_REFERENCE" in os.environ else None
 
 
 @contextmanager
@@ -105,6 +104,8 @@ def rope_table(n, pairs, seed):
 
 
 def main():
+    if REF is None or not (REF / "powershard").is_dir():
+        raise SystemExit("set POWERSHARD_REFERENCE to a ComfyUI-PowerShard source tree")
     sys.path.insert(0, str(REF))
     torch.set_num_threads(4)
     from powershard import wan_model, attention
