@@ -210,6 +210,49 @@ def test_token_mode_over_gloo(world, total, heads, tmp_path, gloo_available):
     assert json.loads(report.read_text())["status"] == "PASS"
 
 
+def wan_entry_worker(rank, world, store, report, total, heads, ulysses):
+    """wan.sequence_attention (the reference's entry, wan_model.py:441-502) on
+    each rank: routes by the shared state's mode and keeps its counters."""
+    oracle = _setup_paths()
+    from powershard_b200 import wan
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(9)
+        q, k, v = (torch.randn(1, total, heads, 128, generator=g) for _ in range(3))
+        a, b = oracle.shard_bounds(total, rank, world)
+        module = type("SelfAttention", (), {})()
+        module.num_heads, module.head_dim = heads, 128
+        module._ps_sequence = dict(total=total, enabled=True, ulysses=ulysses, comm_dtype="fp32",
+                                   kv_collectives=0, kv_gathered_bytes=0, out_collectives=0, out_exchanged_bytes=0)
+        module._ps_b200_engine = UlyssesAttention(kernels=OracleKernels)
+        wire = wan.WIRE_DTYPE
+        wan.WIRE_DTYPE = torch.float32  # the stand-ins compute in fp32: compare tightly
+        try:
+            out = wan.sequence_attention(module, q[:, a:b], k[:, a:b], v[:, a:b])
+        finally:
+            wan.WIRE_DTYPE = wire
+        expected = oracle.sdpa_fp32(q, k, v)[:, a:b]
+        torch.testing.assert_close(out, expected, atol=1e-5, rtol=1e-5)
+        st = module._ps_sequence
+        assert st["kv_collectives"] == 1
+        assert st["out_collectives"] == (1 if ulysses else 0)
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS")))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads,ulysses", [(2, 41, 5, True), (3, 41, 5, False), (2, 9, 3, False)])
+def test_wan_entry_over_gloo(world, total, heads, ulysses, tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    mp.spawn(wan_entry_worker, args=(world, str(tmp_path / "store"), str(report), total, heads, ulysses),
+             nprocs=world, join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
+
+
 def _inputs(total, heads, oracle):
     g = torch.Generator().manual_seed(7)
     x = [torch.randn(1, total, heads * 128, generator=g) for _ in range(3)]
