@@ -109,3 +109,35 @@ def test_error_mapping_to_reference_exceptions():
     rc = lib.ps_b200_unpack(16, 16, 128, _lib.BF16, _lib.BF16, 2, 1, 1, 5, 2, 128, None)
     with pytest.raises(ValueError):
         _lib.check(rc, "unpack")
+
+
+def test_peer_and_token_entries_validate_on_the_host(lib):
+    """The peer-store entry points reject bad tables and sizes before any
+    device work (no GPU needed to see it)."""
+    from powershard_b200 import _lib
+    st = _lib.i64([128, 128, 128])
+    # token fan-out: destination count out of range, null destinations
+    rc = lib.ps_b200_prepass_token_to(16, 16, 16, st, None, 0, 0, _lib.BF16, 0, 0, 16, _lib.ptrs([16]), 0,
+                                      _lib.BF16, 1, 1, 1, 128, 1e-6, 0, 0, 64, None)
+    assert rc == _lib.ERR_INVALID
+    rc = lib.ps_b200_prepass_token_to(16, 16, 16, st, None, 0, 0, _lib.BF16, 0, 0, 16, _lib.ptrs([16, 0]), 2,
+                                      _lib.BF16, 1, 1, 1, 128, 1e-6, 0, 0, 64, None)
+    assert rc == _lib.ERR_INVALID and b"destination 1" in lib.ps_b200_last_error()
+    # broadcast: size not a multiple of 16, misaligned destination
+    assert lib.ps_b200_broadcast(_lib.ptrs([16]), 1, 16, 24, None) == _lib.ERR_INVALID
+    assert lib.ps_b200_broadcast(_lib.ptrs([18]), 1, 16, 32, None) == _lib.ERR_INVALID
+    assert lib.ps_b200_broadcast(_lib.ptrs([16]), 1, 16, 0, None) == _lib.OK  # nothing to copy
+    # joint attention to peer blocks: null table, row stride too small
+    rc = lib.ps_b200_ulysses_joint_attn_to(16, 16, None, 256, 16, _lib.BF16, _lib.BF16, 2, 8, 16, 4, None,
+                                           2, 2, 128, 0.1, None, 0, None, None)
+    assert rc == _lib.ERR_INVALID
+    rc = lib.ps_b200_ulysses_joint_attn_to(16, 16, _lib.ptrs([16, 16]), 128, 16, _lib.BF16, _lib.BF16, 2, 8, 16, 4,
+                                           None, 2, 2, 128, 0.1, None, 0, None, None)
+    assert rc == _lib.ERR_INVALID and b"row stride" in lib.ps_b200_last_error()
+    # strided unpack: misaligned strides
+    assert lib.ps_b200_unpack_strided(16, 12, 256, 16, 256, _lib.BF16, _lib.BF16, 4, 2, 1, 128,
+                                      None) == _lib.ERR_INVALID
+    # split-half RoPE geometry
+    rc = lib.ps_b200_prepass(16, 16, 16, st, None, 16, 16, _lib.BF16, 16, 256, 16, _lib.BF16, 1, 4, 4, 1, 1, 128,
+                             1e-6, 2, 1, 12, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"split-half" in lib.ps_b200_last_error()
