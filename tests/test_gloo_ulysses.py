@@ -337,3 +337,93 @@ def test_rank_leaving_makes_survivor_raise(tmp_path, gloo_available):
     data = json.loads(report.read_text())
     assert data["result"] != "completed", data
     assert data["seconds"] < 60
+
+
+class H3Kernels(OracleKernels):
+    """Stand-ins for the H3 pre-pass: per-head RMSNorm + split-half partial
+    RoPE (powershard/attention.py:98-103, :106-181) before the pack."""
+
+    @staticmethod
+    def _normed(x_q, x_k, x_v, w_q, w_k, freqs, heads, eps, norm_rope, rope_split_pairs):
+        from oracle import ulysses_oracle as oracle
+        from powershard_b200 import ops
+        assert norm_rope == ops.NORM_PER_HEAD and freqs.shape[-3] == rope_split_pairs
+        n = x_q.shape[0]
+        table = freqs[None, :, None]
+        q, k = (oracle.rope_split_half(oracle.rms_norm_heads(x.reshape(1, n, -1), w, heads, eps)[0], table)
+                for x, w in ((x_q, w_q), (x_k, w_k)))
+        return q, k, x_v.reshape(n, heads, -1)
+
+    @classmethod
+    def prepass(cls, x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True, rope_split_pairs=None):
+        from oracle import ulysses_oracle as oracle
+        q, k, v = cls._normed(x_q, x_k, x_v, w_q, w_k, freqs, geo.heads, eps, norm_rope, rope_split_pairs)
+        send.copy_(oracle.pack_qkv(q.to(send.dtype), k.to(send.dtype), v.to(send.dtype), geo.total, geo.rank,
+                                   geo.world))
+
+    @classmethod
+    def token_pack(cls, x_q, x_k, x_v, w_q, w_k, freqs, qkv, n_local, heads, head_dim, eps=1e-6, norm_rope=True,
+                   rope_split_pairs=None):
+        q, k, v = cls._normed(x_q, x_k, x_v, w_q, w_k, freqs, heads, eps, norm_rope, rope_split_pairs)
+        qkv.zero_()
+        for kind, t in enumerate((q, k, v)):
+            qkv[kind, :n_local] = t.to(qkv.dtype)
+
+
+def h3_worker(rank, world, store, report, total, heads, ulysses, pairs):
+    """h3.attention_forward (replacing powershard/attention.py:106-181) on
+    each rank, against per-head norm + split-half RoPE + attention of the
+    whole sequence; the module's projection and output are plain matmuls."""
+    oracle = _setup_paths()
+    from types import SimpleNamespace
+    from powershard_b200 import h3
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(13)
+        dim = 64
+        x = torch.randn(total, dim, generator=g)
+        proj = torch.randn(3 * heads * 128, dim, generator=g) * 0.1
+        wq, wk = torch.rand(128, generator=g) + 0.5, torch.rand(128, generator=g) + 0.5
+        ang = torch.rand(total, pairs, generator=g, dtype=torch.float64) * 30.0
+        c, s = torch.cos(ang), torch.sin(ang)
+        table = torch.stack([c, -s, s, c], -1).reshape(1, total, 1, pairs, 2, 2).float()
+        q, k, v = (x @ proj.t()).split(heads * 128, dim=-1)
+        qn = oracle.rope_split_half(oracle.rms_norm_heads(q[None], wq, heads)[0], table)
+        kn = oracle.rope_split_half(oracle.rms_norm_heads(k[None], wk, heads)[0], table)
+        expected = oracle.sdpa_fp32(qn[None], kn[None], v.reshape(1, total, heads, 128))[0]
+        a, b = oracle.shard_bounds(total, rank, world)
+        module = SimpleNamespace(heads=heads, head_dim=128, qkv_proj=lambda t: t @ proj.t(),
+                                 q_norm=SimpleNamespace(weight=wq, eps=1e-6),
+                                 k_norm=SimpleNamespace(weight=wk, eps=1e-6), out_proj=lambda t: t)
+        state = dict(total=total, enabled=True, ulysses=ulysses, comm_dtype="fp32")
+        h3.install_attention(module, state=state)
+        module._ps_b200_engine = UlyssesAttention(kernels=H3Kernels)
+        wire = h3.WIRE_DTYPE
+        h3.WIRE_DTYPE = torch.float32  # the stand-ins compute in fp32: compare tightly
+        try:
+            out = module.forward(x[a:b], table[:, a:b])
+        finally:
+            h3.WIRE_DTYPE = wire
+        assert out.shape == (b - a, heads * 128)
+        torch.testing.assert_close(out.reshape(b - a, heads, 128), expected[a:b], atol=1e-5, rtol=1e-5)
+        assert state["kv_collectives"] == 1
+        if ulysses:
+            assert state["out_collectives"] == 1 and state["ulysses_local_heads"] == -(-heads // world)
+        else:
+            assert "out_collectives" not in state
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS")))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads,ulysses,pairs", [(2, 41, 5, True, 32), (3, 40, 4, False, 16),
+                                                             (2, 9, 3, False, 64)])
+def test_h3_entry_over_gloo(world, total, heads, ulysses, pairs, tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    mp.spawn(h3_worker, args=(world, str(tmp_path / "store"), str(report), total, heads, ulysses, pairs),
+             nprocs=world, join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
