@@ -10,7 +10,8 @@
 
 Both follow the shared state's mode: Ulysses (``ulysses`` true, the
 default) or token mode (K/V all-gathered, local queries,
-wan_model.py:489-500).
+wan_model.py:489-500).  ``gather_tokens`` is the final-head gather of the
+sequence-parallel forward (wan_model.py:336-340, :1072-1075).
 
 Both read the module attributes the reference installs
 (``install_wan_compute``, wan_model.py:727-768): ``num_heads``,
@@ -25,8 +26,10 @@ from __future__ import annotations
 import types
 
 import torch
+import torch.distributed as dist
 
 from .contract import AttentionOptions, UnsupportedAttention
+from .partition import shard_bounds
 from .ulysses import UlyssesAttention
 
 WIRE_DTYPE = torch.bfloat16
@@ -116,6 +119,36 @@ def sequence_attention(self, q, k, v, total=None):
             _rows(v[b], heads, dim, WIRE_DTYPE), total=total, heads=heads, norm_rope=False,
             out_dtype=torch.float32, state=state if b == 0 else None))
     return torch.stack(outs)
+
+
+def gather_tokens(x, total, dtype=None, group=None):
+    """Batch-first all-gather of token rows: [B, n, ...] -> [B, total, ...].
+
+    The final-head gather of the sequence-parallel Wan forward
+    (powershard/wan_model.py:336-340, called at :1072-1075, where the caller
+    counts ``head_gathers``), with the row semantics of
+    powershard/attention.py:40-54: rank r holds rows shard_bounds(total, r,
+    W); every rank's rows are padded to ceil(total / W), one
+    all_gather_into_tensor (NCCL on the current stream for CUDA tensors)
+    concatenates them in rank order, and the padding is cut.  `dtype` is the
+    wire dtype; the result comes back in x's dtype.  The result is a fresh
+    tensor, never a view of a buffer that a later call rewrites.
+    """
+    world, rank = (dist.get_world_size(group), dist.get_rank(group)) if dist.is_initialized() else (1, 0)
+    a, b = shard_bounds(total, rank, world)
+    if x.shape[1] != b - a:
+        raise ValueError(f"gather_tokens: {x.shape[1]} local tokens, shard_bounds gives {b - a}")
+    wire = dtype or x.dtype
+    width = -(-total // world)
+    rows = x.transpose(0, 1)                       # [n, B, ...] view
+    send = torch.zeros((width,) + tuple(rows.shape[1:]), dtype=wire, device=x.device)
+    send[:b - a].copy_(rows)
+    gathered = torch.empty((world * width,) + tuple(rows.shape[1:]), dtype=wire, device=x.device)
+    if world > 1:
+        dist.all_gather_into_tensor(gathered, send, group=group)
+    else:
+        gathered.copy_(send)
+    return gathered[:total].transpose(0, 1).to(x.dtype).contiguous()
 
 
 def install_self_attention(module, group=None, state: dict | None = None):

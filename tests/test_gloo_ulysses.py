@@ -427,3 +427,45 @@ def test_h3_entry_over_gloo(world, total, heads, ulysses, pairs, tmp_path, gloo_
     mp.spawn(h3_worker, args=(world, str(tmp_path / "store"), str(report), total, heads, ulysses, pairs),
              nprocs=world, join=True)
     assert json.loads(report.read_text())["status"] == "PASS"
+
+
+def gather_worker(rank, world, store, report, total, batch):
+    """wan.gather_tokens (the final-head gather, powershard/wan_model.py:336-340)
+    on each rank against the oracle's gather_rows of every batch row."""
+    oracle = _setup_paths()
+    from powershard_b200 import wan
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        g = torch.Generator().manual_seed(17)
+        full = torch.randn(batch, total, 3, 5, generator=g)
+        bounds = [oracle.shard_bounds(total, r, world) for r in range(world)]
+        a, b = bounds[rank]
+        out = wan.gather_tokens(full[:, a:b], total)
+        expected = torch.stack([oracle.gather_rows([full[i, s:e] for s, e in bounds], total, world)
+                                for i in range(batch)])
+        assert torch.equal(out, expected) and torch.equal(out, full) and out.is_contiguous()
+        # fp16 wire: values come back in x's dtype, rounded through the wire
+        half = wan.gather_tokens(full[:, a:b], total, dtype=torch.float16)
+        assert half.dtype == torch.float32 and torch.equal(half, full.half().float())
+        # a second call never rewrites the first result
+        again = wan.gather_tokens(full[:, a:b] * 2, total)
+        assert torch.equal(out, full) and torch.equal(again, full * 2)
+        try:
+            wan.gather_tokens(torch.zeros(batch, b - a + 1, 3, 5), total)  # raises before any collective
+            raise AssertionError("wrong local token count accepted")
+        except ValueError:
+            pass
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS")))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,batch", [(2, 41, 1), (3, 41, 2), (4, 9, 1)])
+def test_head_gather_over_gloo(world, total, batch, tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    mp.spawn(gather_worker, args=(world, str(tmp_path / "store"), str(report), total, batch), nprocs=world,
+             join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
