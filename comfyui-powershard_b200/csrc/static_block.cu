@@ -6,12 +6,15 @@
 //
 // Its only scratch - the packed q/k/v buffer between the two kernels and the
 // attention kernel's status word - lives in the file-scope array below, of a
-// fixed size.  Every GPU on which this entry point is used holds that array
-// until the process exits.  All calls share it and it keeps the last call's
-// contents: the status word is cleared on the caller's stream at the start of
-// every call (the packed buffer is fully rewritten by the pre-pass), and calls
-// that overlap on the GPU (different streams, or other host threads) race on
-// it.
+// fixed size.  A GPU holds that array from the moment this file's module is
+// loaded on it until the process exits: with the default lazy module loading
+// that is the first call of this entry point on that GPU; with eager loading
+// (CUDA_MODULE_LOADING=EAGER) it is every GPU on which the process creates a
+// CUDA context while the library is loaded.  All calls share the array and
+// it keeps the last call's contents: the status word is cleared on the
+// caller's stream at the start of every call (the packed buffer is fully
+// rewritten by the pre-pass), and calls that overlap on the GPU (different
+// streams, or other host threads) race on it.
 #include "ps_b200.h"
 #include "internal.h"
 
@@ -27,24 +30,55 @@ constexpr size_t kQkvBytes = size_t(96) << 20;  // 96 MiB of packed q/k/v
 static __device__ __align__(256) unsigned char g_static_scratch[kStatusBytes + kQkvBytes];
 
 std::mutex g_mutex;
-void* g_scratch_ptr[64] = {nullptr};
+struct ScratchSlot {
+  CUcontext ctx = nullptr;  // context the address belongs to
+  void* ptr = nullptr;
+};
+ScratchSlot g_scratch[64];
+
+// cuCtxGetCurrent through the runtime's driver entry point (no -lcuda).
+CUresult current_context(CUcontext* ctx) {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(p);
+  });
+  if (!fn) return CUDA_ERROR_NOT_FOUND;
+  return fn(ctx);
+}
 
 // Device address of the scratch array on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is queried
-// with cudaGetSymbolAddress once per device (with that device current).
+// with cudaGetSymbolAddress once per device, with that device current, and
+// again whenever the device's context changed since (after cudaDeviceReset,
+// or when the primary context was released and created anew, the module is
+// loaded again, possibly at another address).
 int scratch_address(unsigned char** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return set_cuda_error("cudaGetDevice", err);
   if (dev < 0 || dev >= 64) return set_error(PS_B200_ERR_UNSUPPORTED, "device index %d above 63", dev);
+  // The context current before the lookup (null while the runtime has not
+  // made one current on this thread yet).
+  CUcontext ctx = nullptr;
+  if (current_context(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_scratch_ptr[dev]) {
+  ScratchSlot& slot = g_scratch[dev];
+  if (!slot.ptr || !ctx || slot.ctx != ctx) {
     void* p = nullptr;
-    err = cudaGetSymbolAddress(&p, g_static_scratch);
+    err = cudaGetSymbolAddress(&p, g_static_scratch);  // also makes the primary context current
     if (err != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(static scratch)", err);
-    g_scratch_ptr[dev] = p;
+    if (current_context(&ctx) != CUDA_SUCCESS || !ctx)
+      return set_error(PS_B200_ERR_CUDA, "static block: no current CUDA context on device %d", dev);
+    slot.ptr = p;
+    slot.ctx = ctx;
   }
-  *out = static_cast<unsigned char*>(g_scratch_ptr[dev]);
+  *out = static_cast<unsigned char*>(slot.ptr);
   return PS_B200_OK;
 }
 
@@ -61,6 +95,10 @@ extern "C" int ps_b200_block_fwd_static(const void* x_q, const void* x_k, const 
   if (dtype != PS_B200_BF16 && dtype != PS_B200_FP16)
     return set_error(PS_B200_ERR_UNSUPPORTED, "static block supports bf16 and fp16 inputs only");
   if (n < 0 || heads < 1 || head_dim <= 0) return set_error(PS_B200_ERR_INVALID, "inconsistent block geometry");
+  // The attention kernel computes head_dim 128 only: refuse anything else
+  // before any work is queued on the shared scratch.
+  if (head_dim != 128)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "static block supports head_dim 128 only (got %d)", head_dim);
   const size_t need = size_t(3) * size_t(n) * size_t(heads) * size_t(head_dim) * 2;
   if (need > kQkvBytes)
     return set_error(PS_B200_ERR_UNSUPPORTED,

@@ -305,15 +305,19 @@ int ps_b200_selftest_bounded_wait(int* status, int limit_us, void* stream);
  * its own pool, or a step that must not hit cudaMalloc's implicit device
  * synchronisation.  Same math as ps_b200_prepass (world 1, norm_rope 1)
  * followed by ps_b200_ulysses_attn_fwd (world 1): out [n][heads][head_dim]
- * in out_dtype.  Its scratch (packed q/k/v and the status word) is a fixed
- * 96 MiB static device array, so 6 * n * heads * head_dim <= 96 MiB
- * (n * heads <= 131072 at head_dim 128); larger requests return
- * PS_B200_ERR_UNSUPPORTED.  Every GPU that uses this entry point keeps the
- * array until exit.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress), so make it before any stream capture.
- * Calls share the array: calls that overlap on the GPU race.  If host_status
- * is not NULL the call synchronizes the stream and stores the kernel's
- * device status there (0 = ok); with NULL it stays asynchronous.
+ * in out_dtype, head_dim 128 only.  Its scratch (packed q/k/v and the status
+ * word) is a fixed 96 MiB static device array, so 6 * n * heads * head_dim
+ * <= 96 MiB (n * heads <= 131072 at head_dim 128); larger requests return
+ * PS_B200_ERR_UNSUPPORTED before any work is queued.  A GPU holds the array
+ * from the first call on it (with CUDA_MODULE_LOADING=EAGER: from the
+ * creation of the process's context on it) until the process exits.  The
+ * first call on a device (and the first after that device's context was
+ * reset) looks up the array's device address (cudaGetSymbolAddress), so
+ * make it before any stream capture.  Calls share the array: calls that
+ * overlap on the GPU race.  If host_status is not NULL the call synchronizes
+ * the stream and stores the kernel's device status there (0 = ok).  With
+ * NULL it stays asynchronous and reports no device-side abort: the status
+ * word lives in the shared array and the next call clears it.
  */
 int ps_b200_block_fwd_static(const void* x_q, const void* x_k, const void* x_v, const int64_t x_row_strides[3],
                              const void* w_qnorm, const void* w_knorm, int w_dtype, const float* freqs,

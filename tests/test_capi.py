@@ -141,3 +141,15 @@ def test_peer_and_token_entries_validate_on_the_host(lib):
     rc = lib.ps_b200_prepass(16, 16, 16, st, None, 16, 16, _lib.BF16, 16, 256, 16, _lib.BF16, 1, 4, 4, 1, 1, 128,
                              1e-6, 2, 1, 12, None)
     assert rc == _lib.ERR_UNSUPPORTED and b"split-half" in lib.ps_b200_last_error()
+
+
+def test_static_block_rejects_head_dim_before_any_work(lib):
+    """The allocation-free block computes head_dim 128 only; another head size
+    is refused on the host, before the shared scratch is looked up or any work
+    is queued on it."""
+    from powershard_b200 import _lib
+    rc = lib.ps_b200_block_fwd_static(16, 16, 16, _lib.i64([64, 64, 64]), 16, 16, _lib.FP32, 16, 128, 16,
+                                      _lib.BF16, _lib.BF16, 100, 1, 64, 1e-6, 0.125, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    assert b"head_dim 128" in lib.ps_b200_last_error()
+    assert lib.ps_b200_kernel_launches() == 0
