@@ -24,7 +24,20 @@ roofline = the attention kernel's achieved TFLOP/s (CUDA events around each
 launch) against the measured bf16 peak; cpu_baseline = the CPU oracle's
 restatement of the reference algorithm on a bounded sample (N=1 only).
 ``--impl reference`` times only that CPU restatement (rank 0; other ranks
-exit 0).
+exit 0): every step is a bounded, proportional slice of the layer whose
+wall time is measured (nothing inside a step is extrapolated).
+
+Outside the timed regions every rank also reports:
+  parity  this rank's output against a plain PyTorch fp32 restatement of the
+          block (RMSNorm, RoPE, softmax attention) on sampled rows of every
+          head, and, at N > 1, the peer-exchange output against the NCCL
+          all_to_all exchange (bit-identical); the run exits non-zero when
+          parity fails;
+  sdpa    torch scaled_dot_product_attention (cuDNN) on the same bf16
+          tensors this rank's attention kernel reads, timed the same way;
+  comm    (N > 1) bytes each rank sends across NVLink per step and what each
+          exchange costs: the peer stores of the fused kernels against the
+          same kernels storing locally, and NCCL all_to_all_single.
 """
 from __future__ import annotations
 
@@ -85,6 +98,10 @@ def peaks():
     return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s"
 
 
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one attention launch at L=8192 "
+                  "(profiles/ncu_traffic.txt), scaled by tokens and by heads per rank; not measured at full size")
+
+
 def traffic_per_launch(world):
     """dram read+write bytes per attention launch from the committed ncu summary."""
     path = ROOT / "profiles" / "ncu_traffic.txt"
@@ -135,30 +152,263 @@ class ClockSampler:
                     reasons=reasons, samples=len(sm))
 
 
+def config0_baseline(cores):
+    """configs[0] (Wan2.1-1.3B-shaped layer) over gloo W=2 on the host cores:
+    the whole layer of the reference's CPU chain, restated, measured end to
+    end per provider, and the committed ratio of that restatement's time to
+    the reference's own code measured on the build machine."""
+    from oracle import cpu_layer
+    res = cpu_layer.time_layer_gloo(world=2, threads=max(1, cores // 2), steps=3, warmup=1)
+    pin = ROOT / "oracle" / "config0_timing.json"
+    if pin.exists():
+        data = json.loads(pin.read_text())
+        res["port_vs_reference_code"] = {k: dict(port_over_reference_time=v["port_over_reference_time"],
+                                                 max_abs_output_diff=v["max_abs_output_diff"])
+                                         for k, v in data["providers"].items()}
+        res["port_vs_reference_code"]["measured_on"] = f"{data['cpu_model']}, {data['cores']} cores"
+    res["workload"] = "BASELINE configs[0]: x [1, 4096, 1536] fp32, 12x128, q/k/v/o Linear, gloo W=2, whole layer"
+    return res
+
+
 def reference_arm(args, world, rank):
+    """The reference's CPU algorithm (oracle restatement, bit-exact to the
+    reference's own code on configs[0]) on the host cores.  Each step is a
+    bounded slice of the configs[1] layer whose wall time is measured."""
     if rank != 0:
         return
     import __graft_entry__  # noqa: F401
     from oracle import ulysses_oracle as oracle
     cores = len(os.sched_getaffinity(0))
-    budget = max(1.0, min(10.0, 150.0 / (args.steps + args.warmup)))
-    values = []
+    budget = max(1.0, min(6.0, 150.0 / (args.steps + args.warmup)))
+    rates, walls = [], []
     last = None
+    t_run = time.perf_counter()
     for step in range(args.warmup + args.steps):
-        last = oracle.time_reference_sample(TOTAL, HEADS, DIM, budget_s=budget, threads=cores, seed=step)
+        last = oracle.time_reference_step(TOTAL, HEADS, DIM, budget_s=budget, threads=cores, seed=step)
         if step >= args.warmup:
-            values.append(last["tflops"])
-    value = statistics.median(values)
-    sample = (f"per step: full pre-pass over {TOTAL} tokens + math_attention (128x512 fp32 tiles) for "
-              f"{last['attention_chunks']} of {last['attention_chunks_total']} query chunks (head 0 vs all keys), "
-              f"extrapolated to the layer")
+            rates.append(last["tflops"])
+            walls.append(last["wall_s"])
+    value = statistics.median(rates)
+    sample = (f"per step: math_attention (128x512 fp32 tiles) for {last['chunks']} of {last['chunks_total']} "
+              f"(query chunk, head) units against all {TOTAL} keys + the q/k RMSNorm/RoPE/pack pre-pass of "
+              f"the same fraction ({last['tokens']} tokens); rate = attention FLOPs executed / step wall time")
+    cfg0 = config0_baseline(cores)
     line = dict(metric=METRIC, value=value, unit=UNIT, impl="reference", n_gpus=args.gpus, steps=args.steps,
-                warmup=args.warmup, ms_per_step=FLOPS / (value * 1e12) * 1e3, higher_is_better=True,
+                warmup=args.warmup, ms_per_step=statistics.median(walls) * 1e3,
+                ms_per_layer_extrapolated=FLOPS / (value * 1e12) * 1e3, higher_is_better=True,
                 scaling="strong", vs_baseline=None, dtype="f32", data="synthetic",
+                hardware=f"host CPU only ({cores} threads), no GPU work",
                 config=workload_config(args.gpus),
-                cpu_baseline=dict(value=value, unit=UNIT, cores=last["threads"], kind="port", sample=sample),
-                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+                cpu_baseline=dict(value=value, unit=UNIT, cores=last["threads"], kind="port", sample=sample,
+                                  config0_gloo_w2=cfg0),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                run_s=time.perf_counter() - t_run)
     print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- fp32 check
+def fp32_block_rows(q_rows, k_all, v_all, w, freqs_rows, freqs_all, heads, eps=1e-6):
+    """Plain PyTorch fp32 restatement of the block for a few query rows:
+    RMSNorm over the full width (rounded to the projection dtype, as the
+    reference's RMSNorm returns it), interleaved-pair RoPE in fp32, softmax
+    attention in fp32 over every key.  q_rows [R, H*D], k_all/v_all [L, H*D]
+    projections; returns [R, H, D] fp32."""
+    def norm_rope(x, table):
+        xf = x.float()
+        y = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype).float()
+        y = y.view(x.shape[0], heads, -1, 1, 2)                      # [n, H, D/2, 1, 2]
+        rot = table[:, None]                                         # [n, 1, D/2, 2, 2]
+        return (rot[..., 0] * y[..., 0] + rot[..., 1] * y[..., 1]).reshape(x.shape[0], heads, -1)
+    q = norm_rope(q_rows, freqs_rows)
+    k = norm_rope(k_all, freqs_all)
+    v = v_all.float().view(v_all.shape[0], heads, -1)
+    scale = q.shape[-1] ** -0.5
+    s = torch.einsum("rhd,lhd->hrl", q, k) * scale
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hrl,lhd->rhd", p, v)
+
+
+def sample_rows(n, count, seed):
+    """Row indices of a shard: first and last rows, 128-row tile edges and an
+    even spread, `count` in all."""
+    fixed = {0, 1, 2, n - 3, n - 2, n - 1, 127, 128, 255, 256, n // 2}
+    rows = sorted(r for r in fixed if 0 <= r < n)
+    g = torch.Generator().manual_seed(seed)
+    extra = torch.randperm(n, generator=g).tolist()
+    for r in extra:
+        if len(rows) >= min(count, n):
+            break
+        if r not in rows:
+            rows.append(r)
+    return sorted(rows)
+
+
+def check_parity(engine_out, proj, norm_w, geo, grid, world, rank, dev, nccl_out=None, rows_per_rank=64):
+    """Max-abs / mean-rel error of this rank's output rows (all heads) against
+    the fp32 restatement; bit-identity with the NCCL exchange when given."""
+    total, heads = geo.total, geo.heads
+    from powershard_b200.partition import shard_bounds
+    from powershard_b200.rope import rope_table_3d
+    freqs_all = rope_table_3d(grid, DIM, device=dev)[:total]
+    n = geo.n_local
+    width = geo.width
+    if world > 1:
+        gathered = []
+        for t in proj[1:]:
+            pad = torch.zeros((width, t.shape[1]), dtype=t.dtype, device=dev)
+            pad[:n] = t
+            full = torch.empty((world * width, t.shape[1]), dtype=t.dtype, device=dev)
+            dist.all_gather_into_tensor(full, pad)
+            parts = []
+            for r in range(world):
+                ra, rb = shard_bounds(total, r, world)
+                parts.append(full[r * width: r * width + (rb - ra)])
+            gathered.append(torch.cat(parts))
+        k_all, v_all = gathered
+    else:
+        k_all, v_all = proj[1], proj[2]
+    a, _ = geo.bounds
+    rows = sample_rows(n, rows_per_rank, seed=rank)
+    idx = torch.tensor(rows, device=dev)
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = fp32_block_rows(proj[0][idx], k_all, v_all, norm_w, freqs_all[a + idx], freqs_all, heads)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+    got = engine_out[idx].float()
+    err = (got - ref).abs()
+    stats = torch.tensor([float(err.max()), float(err.sum()), float(ref.abs().sum()),
+                          0.0 if nccl_out is None or torch.equal(engine_out, nccl_out) else 1.0],
+                         device=dev, dtype=torch.float64)
+    maxes = stats.clone()
+    sums = stats.clone()
+    if world > 1:
+        dist.all_reduce(maxes, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+    max_abs = float(maxes[0])
+    mean_rel = float(sums[1] / sums[2])
+    identical = None if nccl_out is None else bool(maxes[3] == 0.0)
+    ok = max_abs <= 2e-2 and mean_rel <= 5e-3 and identical is not False
+    return dict(ok=ok, max_abs=max_abs, mean_rel=mean_rel, tolerance=dict(max_abs=2e-2, mean_rel=5e-3),
+                rows_checked_per_rank=len(rows), heads_checked=heads, ranks=world,
+                identical_peer_vs_nccl=identical,
+                reference="plain PyTorch fp32 RMSNorm + RoPE + softmax attention over all keys")
+
+
+def received_qkv(engine, geo, dev):
+    """This rank's post-exchange q/k/v [1, h_valid, L, D] (contiguous copies of
+    the receive buffer the attention kernel reads)."""
+    px = engine._peer(geo, torch.bfloat16, dev)
+    recv = px.recv if px is not None else engine._workspace(geo, torch.bfloat16, dev)[0]["recv"]
+    w, _, width, h, d = recv.shape
+    hv = geo.heads_valid
+    out = []
+    for i in range(3):
+        t = recv[:, i].reshape(w * width, h, d)[:geo.total, :hv]
+        out.append(t.permute(1, 0, 2).unsqueeze(0).contiguous())
+    return out
+
+
+def time_events(fn, reps, warm=2):
+    for _ in range(warm):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def time_sdpa(q, k, v):
+    """torch SDPA (cuDNN backend if it runs, else flash) on this rank's heads."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import torch.nn.functional as F
+    for backend in (SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION):
+        try:
+            with sdpa_kernel([backend]):
+                ms = time_events(lambda: F.scaled_dot_product_attention(q, k, v), reps=5)
+            return ms, str(backend).split(".")[-1]
+        except RuntimeError:
+            continue
+    return None, "unavailable"
+
+
+def measure_comm(engine, proj, norm_w, freqs, geo, dev, ms_step, attn_ms):
+    """Per-rank NVLink bytes of one step and the cost of each exchange (max
+    over ranks): the fused kernels storing into peers against the same
+    kernels storing locally, and NCCL all_to_all_single of the same buffers."""
+    from powershard_b200 import ops
+    world = geo.world
+    esize = 2
+    block_qkv = 3 * geo.width * geo.heads_per_rank * DIM * esize
+    block_out = geo.width * geo.heads_per_rank * DIM * esize
+    qkv_bytes, out_bytes = (world - 1) * block_qkv, (world - 1) * block_out
+    local_send = torch.empty(geo.send_shape(), dtype=torch.bfloat16, device=dev)
+    local_stage = torch.empty((geo.width, geo.padded_heads, DIM), dtype=torch.bfloat16, device=dev)
+    status = ops.DeviceStatus(dev)
+    ws = ops.attention_workspace(dev)
+    scale = DIM ** -0.5
+    res = {}
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[dev.index])
+
+    px = engine._peer(geo, torch.bfloat16, dev)
+    if px is not None:
+        local_blocks = [local_stage.data_ptr() + r * geo.heads_per_rank * DIM * esize for r in range(world)]
+        sync_all()
+        t_pre_to = time_events(lambda: ops.prepass_to(*proj, norm_w, norm_w, freqs, px.dst_blocks, geo,
+                                                      torch.bfloat16), reps=5)
+        sync_all()
+        t_pre_loc = time_events(lambda: ops.prepass(*proj, norm_w, norm_w, freqs, local_send, geo), reps=5)
+        sync_all()
+        t_att_to = time_events(lambda: ops.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride,
+                                                                torch.bfloat16, geo, scale, status, workspace=ws),
+                               reps=3, warm=1)
+        sync_all()
+        t_att_loc = time_events(lambda: ops.ulysses_attention_to(px.recv, local_blocks, px.out_row_stride,
+                                                                 torch.bfloat16, geo, scale, status, workspace=ws),
+                                reps=3, warm=1)
+        sync_all()
+        res["peer"] = dict(prepass_to_ms=t_pre_to, prepass_local_ms=t_pre_loc, attn_to_ms=t_att_to,
+                           attn_local_ms=t_att_loc)
+    recv = torch.empty_like(local_send)
+    out_send = torch.empty(geo.out_shape(), dtype=torch.bfloat16, device=dev)
+    out_recv = torch.empty_like(out_send)
+    sync_all()
+    t_a2a_qkv = time_events(lambda: dist.all_to_all_single(recv, local_send), reps=5)
+    sync_all()
+    t_a2a_out = time_events(lambda: dist.all_to_all_single(out_recv, out_send), reps=5)
+    sync_all()
+    res["nccl"] = dict(qkv_a2a_ms=t_a2a_qkv, out_a2a_ms=t_a2a_out)
+    status.check()
+    # max over ranks of every time
+    keys = [(k, kk) for k in res for kk in res[k]]
+    vals = torch.tensor([res[k][kk] for k, kk in keys], device=dev, dtype=torch.float64)
+    dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    for (k, kk), v in zip(keys, vals.tolist()):
+        res[k][kk] = v
+    gbs = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9 if ms and ms > 0 else None  # noqa: E731
+    if "peer" in res:
+        pr = res["peer"]
+        pr["qkv_added_ms"] = pr["prepass_to_ms"] - pr["prepass_local_ms"]
+        pr["out_added_ms"] = pr["attn_to_ms"] - pr["attn_local_ms"]
+        pr["qkv_gbs_over_kernel"] = gbs(qkv_bytes, pr["prepass_to_ms"])
+        pr["out_gbs_over_kernel"] = gbs(out_bytes, pr["attn_to_ms"])
+    nc = res["nccl"]
+    nc["qkv_gbs"] = gbs(qkv_bytes, nc["qkv_a2a_ms"])
+    nc["out_gbs"] = gbs(out_bytes, nc["out_a2a_ms"])
+    res.update(qkv_bytes_per_rank=qkv_bytes, out_bytes_per_rank=out_bytes,
+               link_gbs_nominal=900.0, link_gbs_measured_peer_copy=770.0,
+               step_minus_attention_ms=ms_step - attn_ms,
+               note="bytes each rank sends to the other ranks per step (bf16 wire); GB/s = bytes / time of "
+                    "the step that moves them; added_ms = peer-storing kernel minus the same kernel storing "
+                    "locally")
+    return res
 
 
 def workload_config(world, total=TOTAL):
@@ -321,26 +571,53 @@ def main():
     attn_flops = 4.0 * total * total * geo.heads_valid * DIM
     achieved = attn_flops / (attn_ms * 1e-3) / 1e12
     traffic = traffic_per_launch(world)
+
+    # ---- outside the timed regions: parity, SDPA on the same tensors, comm.
+    out_main = step(proj)
+    nccl_out = None
+    if world > 1 and exchange == "peer":
+        nccl_engine = UlyssesAttention(exchange="nccl")
+        nccl_out = nccl_engine.forward(*proj, norm_w, norm_w, freqs, total=total, heads=HEADS)
+        nccl_engine.check()
+    engine.check()
+    parity = check_parity(out_main, proj, norm_w, geo, grid, world, rank, dev, nccl_out=nccl_out)
+    del nccl_out
+    q_s, k_s, v_s = received_qkv(engine, geo, dev)
+    sdpa_ms, sdpa_backend = time_sdpa(q_s, k_s, v_s)
+    del q_s, k_s, v_s
+    sdpa_vals = torch.tensor([sdpa_ms if sdpa_ms is not None else -1.0], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(sdpa_vals, op=dist.ReduceOp.MAX)
+    sdpa_ms = float(sdpa_vals[0]) if float(sdpa_vals[0]) > 0 else None
+    sdpa = dict(backend=sdpa_backend, ms_per_launch=sdpa_ms,
+                tflops=attn_flops / (sdpa_ms * 1e-3) / 1e12 if sdpa_ms else None,
+                kernel_over_sdpa_time=attn_ms / sdpa_ms if sdpa_ms else None,
+                what="torch scaled_dot_product_attention on this rank's post-exchange q/k/v [1, h, L, 128] bf16, "
+                     "CUDA events, max over ranks")
+    comm = measure_comm(engine, proj, norm_w, freqs, geo, dev, ms, attn_ms) if world > 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import ulysses_oracle as oracle  # the CPU baseline leg only
         cores = len(os.sched_getaffinity(0))
-        res = oracle.time_reference_sample(TOTAL, HEADS, DIM, budget_s=args.cpu_budget, threads=cores)
+        res = oracle.time_reference_step(TOTAL, HEADS, DIM, budget_s=args.cpu_budget, threads=cores)
         cpu = dict(value=res["tflops"], unit=UNIT, cores=res["threads"], kind="port",
-                   sample=(f"full pre-pass over {TOTAL} tokens ({res['prepass_s']:.1f} s) + math_attention "
-                           f"(128x512 fp32 tiles) for {res['attention_chunks']} of {res['attention_chunks_total']} "
-                           f"query chunks of head 0 vs all keys ({res['attention_sample_s']:.1f} s), extrapolated "
-                           f"to the layer: {res['seconds_per_layer']:.0f} s/layer"))
+                   sample=(f"math_attention (128x512 fp32 tiles) for {res['chunks']} of {res['chunks_total']} "
+                           f"(query chunk, head) units against all {TOTAL} keys + the pre-pass of the same "
+                           f"fraction ({res['tokens']} tokens), {res['wall_s']:.1f} s measured; the layer at "
+                           f"this rate: {FLOPS / (res['tflops'] * 1e12):.0f} s"),
+                   config0_gloo_w2=config0_baseline(cores))
     if rank == 0:
         line = dict(
             metric=METRIC, value=flops / (ms * 1e-3) / 1e12, unit=UNIT, n_gpus=world, steps=args.steps,
             warmup=args.warmup, ms_per_step=ms, ms_per_layer=ms, higher_is_better=True, scaling="strong",
             vs_baseline=None, dtype="bf16",
             data="synthetic: x~N(0,1) projected by W~N(0,0.02) (setup), RMSNorm weight 1, RoPE theta 1e4 on 21x30x52",
-            config=dict(workload_config(world, total), exchange=exchange),
+            config=workload_config(world, total), exchange=exchange,
             roofline=dict(bound="tensor", achieved=achieved, peak=peak, unit="TFLOP/s", frac=achieved / peak,
-                          traffic=traffic, kernel="attn_fwd_kernel", attn_ms_per_launch=attn_ms,
-                          flops_per_launch=attn_flops, peak_source=peak_src),
+                          traffic=traffic, traffic_source=TRAFFIC_SOURCE, kernel="attn_fwd_kernel",
+                          attn_ms_per_launch=attn_ms, flops_per_launch=attn_flops, peak_source=peak_src),
+            parity=parity, sdpa=sdpa, comm=comm,
             cpu_baseline=cpu,
             e2e=dict(value=flops / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,
                      h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
@@ -351,6 +628,8 @@ def main():
         dist.barrier(device_ids=[local])
         engine.close()
         dist.destroy_process_group()
+    if not parity["ok"]:
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -282,8 +282,19 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
                    const float* freqs, int64_t freqs_row_stride, void* const* dst, int dtype,
                    int world, int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
                    int norm_rope, int rope_style, int rope_pairs, void* stream, void* q_out = nullptr,
-                   int kv_fanout = 0) {
+                   int kv_fanout = 0, int batch = 1, const int64_t* x_batch_strides = nullptr,
+                   int64_t freqs_batch_stride = 0) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "prepass supports bf16 and fp16 only");
+  if (batch < 0 || batch > 65535) return set_error(PS_B200_ERR_INVALID, "batch must be in [0, 65535]");
+  if (batch == 0) return PS_B200_OK;
+  if (batch > 1) {
+    if (!x_batch_strides) return set_error(PS_B200_ERR_INVALID, "batch > 1 needs x_batch_strides");
+    for (int i = 0; i < 3; ++i)
+      if (x_batch_strides[i] < 0 || x_batch_strides[i] % 8 != 0)
+        return set_error(PS_B200_ERR_INVALID, "x_batch_strides must be non-negative multiples of 8");
+    if (freqs_batch_stride < 0 || freqs_batch_stride % 4 != 0)
+      return set_error(PS_B200_ERR_INVALID, "freqs_batch_stride must be a non-negative multiple of 4");
+  }
   if (world < 1 || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
       int64_t(heads_per_rank) * world < heads || head_dim <= 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent prepass geometry");
@@ -327,9 +338,12 @@ static int prepass_common(const void* x_q, const void* x_k, const void* x_v, con
   a.x[1] = x_k;
   a.x[2] = x_v;
   for (int i = 0; i < 3; ++i) {
+    a.x_batch_stride[i] = (batch > 1 && x_batch_strides) ? x_batch_strides[i] : 0;
     a.x_row_stride[i] = x_row_strides ? x_row_strides[i] : 0;
     a.x_head_stride[i] = x_head_strides ? x_head_strides[i] : head_dim;
   }
+  a.freqs_batch_stride = batch > 1 ? freqs_batch_stride : 0;
+  a.batch = batch;
   a.w[0] = w_qnorm;
   a.w[1] = w_knorm;
   a.w_fp32 = w_dtype == PS_B200_FP32;
@@ -497,25 +511,56 @@ int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t o
                             int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
                             int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, void* workspace,
                             size_t workspace_bytes, int* status, void* stream) {
+  return ps_b200_ulysses_attn_batch(recv, out_blocks, 0, out_row_stride, dtype, out_dtype, 1, world, seg_rows,
+                                    total, seg_valid, heads_per_rank, heads_valid, head_dim, softmax_scale,
+                                    workspace, workspace_bytes, status, stream);
+}
+
+int ps_b200_ulysses_attn_batch(const void* recv, void* const* out_blocks, int64_t out_batch_stride,
+                               int64_t out_row_stride, int dtype, int out_dtype, int batch, int world, int seg_rows,
+                               int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                               float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                               void* stream) {
   if (world < 1 || seg_rows < 0 || total < 0 || heads_per_rank < 1 || heads_valid < 0 ||
-      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total)
+      heads_valid > heads_per_rank || int64_t(seg_rows) * world < total || batch < 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent Ulysses geometry");
   if (int rc = check_seg_valid(seg_valid, world, seg_rows, total)) return rc;
-  if (total == 0 || heads_valid == 0) return PS_B200_OK;
+  if (total == 0 || heads_valid == 0 || batch == 0) return PS_B200_OK;
   if (!out_blocks) return set_error(PS_B200_ERR_INVALID, "null output table");
   if (out_row_stride < int64_t(heads_valid) * head_dim)
     return set_error(PS_B200_ERR_INVALID, "output row stride below heads_valid * head_dim");
-  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows;
-  const int64_t block = n * h * D;
+  if (batch > 1 && out_batch_stride < 0) return set_error(PS_B200_ERR_INVALID, "negative output batch stride");
+  const int64_t D = head_dim, h = heads_per_rank, n = seg_rows, B = batch;
+  const int64_t block = n * h * D;  // one [seg_rows][h][D] block of one batch row
   const char* base = static_cast<const char*>(recv);
-  const int64_t in_st[4] = {int64_t(world) * 3 * block, 3 * block, h * D, D};
-  const int64_t out_st[4] = {0, 0, out_row_stride, D};
+  // recv [world][3][batch][seg_rows][h][D]: strides {batch, segment, row, head}
+  const int64_t in_st[4] = {block, 3 * B * block, h * D, D};
+  const int64_t out_st[4] = {batch > 1 ? out_batch_stride : 0, 0, out_row_stride, D};
   SegTensor tq{base, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  SegTensor tk{base + block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  SegTensor tv{base + block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
-  return attention_common(tq, tk, tv, nullptr, out_st, dtype, out_dtype, 1, heads_valid, 1, head_dim, seg_rows,
+  SegTensor tk{base + B * block * 2, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  SegTensor tv{base + B * block * 4, {in_st[0], in_st[1], in_st[2], in_st[3]}, heads_per_rank};
+  return attention_common(tq, tk, tv, nullptr, out_st, dtype, out_dtype, batch, heads_valid, 1, head_dim, seg_rows,
                           world, total, seg_rows, world, total, softmax_scale, workspace, workspace_bytes, status,
                           stream, nullptr, seg_valid, out_blocks);
+}
+
+int ps_b200_prepass_batch(const void* x_q, const void* x_k, const void* x_v, const int64_t x_batch_strides[3],
+                          const int64_t x_row_strides[3], const int64_t x_head_strides[3], const void* w_qnorm,
+                          const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_batch_stride,
+                          int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int batch, int world,
+                          int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
+                          int norm_rope, int rope_style, int rope_pairs, void* stream) {
+  if (world < 1 || world > kMaxSegs) return set_error(PS_B200_ERR_INVALID, "world must be in [1, %d]", kMaxSegs);
+  if (seg_rows > 0 && batch > 0) {
+    if (!dst_blocks) return set_error(PS_B200_ERR_INVALID, "null destination table");
+    for (int d = 0; d < world; ++d)
+      if (!dst_blocks[d] || !aligned16(dst_blocks[d]))
+        return set_error(PS_B200_ERR_INVALID, "destination block %d null or not 16-byte aligned", d);
+  }
+  return prepass_common(x_q, x_k, x_v, x_row_strides, x_head_strides, w_qnorm, w_knorm, w_dtype, freqs,
+                        freqs_row_stride, dst_blocks, dtype, world, n_local, seg_rows, heads, heads_per_rank,
+                        head_dim, eps, norm_rope, rope_style, rope_pairs, stream, nullptr, 0, batch,
+                        x_batch_strides, freqs_batch_stride);
 }
 
 int ps_b200_ulysses_joint_attn_fwd(const void* recv, const void* prefix_qkv, void* out_send, void* prefix_out,
@@ -569,24 +614,36 @@ int ps_b200_unpack(const void* recv, void* out, int64_t out_row_stride, int dtyp
 int ps_b200_unpack_strided(const void* recv, int64_t src_stride, int64_t row_stride, void* out,
                            int64_t out_row_stride, int dtype, int out_dtype, int n_local, int heads,
                            int heads_per_rank, int head_dim, void* stream) {
+  return ps_b200_unpack_batch(recv, src_stride, 0, row_stride, out, 0, out_row_stride, dtype, out_dtype, 1,
+                              n_local, heads, heads_per_rank, head_dim, stream);
+}
+
+int ps_b200_unpack_batch(const void* recv, int64_t src_stride, int64_t batch_stride, int64_t row_stride, void* out,
+                         int64_t out_batch_stride, int64_t out_row_stride, int dtype, int out_dtype, int batch,
+                         int n_local, int heads, int heads_per_rank, int head_dim, void* stream) {
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "unpack supports bf16 and fp16 inputs only");
   if (out_dtype != dtype && out_dtype != PS_B200_FP32)
     return set_error(PS_B200_ERR_UNSUPPORTED, "unpack output must be fp32 or the input dtype");
-  if (n_local < 0 || heads < 1 || heads_per_rank < 1 || head_dim <= 0 || head_dim % 8 != 0)
+  if (n_local < 0 || batch < 0 || heads < 1 || heads_per_rank < 1 || head_dim <= 0 || head_dim % 8 != 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent unpack geometry");
-  if (int64_t(n_local) * heads * (head_dim / 8) >= (int64_t(1) << 31))
+  if (int64_t(batch) * n_local * heads * (head_dim / 8) >= (int64_t(1) << 31))
     return set_error(PS_B200_ERR_UNSUPPORTED, "unpack size above 2^31 vectors");
-  if (n_local == 0) return PS_B200_OK;
+  if (n_local == 0 || batch == 0) return PS_B200_OK;
   if (!recv || !out || !aligned16(recv) || !aligned16(out) || out_row_stride % 8 != 0 || out_row_stride < 0 ||
-      src_stride % 8 != 0 || src_stride < 0 || row_stride % 8 != 0 || row_stride < 0)
+      src_stride % 8 != 0 || src_stride < 0 || row_stride % 8 != 0 || row_stride < 0 ||
+      (batch > 1 && (batch_stride % 8 != 0 || batch_stride < 0 || out_batch_stride % 8 != 0 ||
+                     out_batch_stride < 0)))
     return set_error(PS_B200_ERR_INVALID, "unpack buffers must be 16-byte aligned, strides %% 8 == 0");
   if (int rc = check_device()) return rc;
   UnpackArgs a{};
   a.recv = recv;
   a.src_stride = src_stride;
+  a.batch_stride = batch > 1 ? batch_stride : 0;
   a.row_stride = row_stride;
   a.out = out;
+  a.out_batch_stride = batch > 1 ? out_batch_stride : 0;
   a.out_row_stride = out_row_stride;
+  a.batch = batch;
   a.world = (heads + heads_per_rank - 1) / heads_per_rank;
   a.n_local = n_local;
   a.seg_rows = n_local;

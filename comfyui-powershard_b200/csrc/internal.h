@@ -60,23 +60,25 @@ int launch_attention(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
 void count_launch();
 
 struct PrepassArgs {
-  const void* x[3];        // q, k, v projection outputs, [n_local][heads*head_dim]
+  const void* x[3];        // q, k, v projection outputs, [batch][n_local][heads*head_dim]
+  int64_t x_batch_stride[3]; // elements between consecutive batch rows
   int64_t x_row_stride[3]; // elements between consecutive tokens
   int64_t x_head_stride[3];// elements between consecutive heads of a token (head_dim: [n][H*D] rows)
   const void* w[2];        // RMSNorm weights of q and k, [heads*head_dim]
   int w_fp32;              // 1: weights are fp32, 0: same 16-bit type as x
-  const float* freqs;      // [n_local][head_dim/2][2][2] fp32
+  const float* freqs;      // [batch][n_local][head_dim/2][2][2] fp32
+  int64_t freqs_batch_stride; // floats between consecutive batch rows (0: one table for the batch)
   int64_t freqs_row_stride;// floats between consecutive tokens
-  void* dst[kMaxSegs];     // block [3][seg_rows][heads_per_rank][head_dim] for each destination rank:
-                           // slices of the local send buffer, or peers' receive buffers
-  int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
+  void* dst[kMaxSegs];     // block [3][batch][seg_rows][heads_per_rank][head_dim] for each destination
+                           // rank: slices of the local send buffer, or peers' receive buffers
+  int batch, world, n_local, seg_rows, heads, heads_per_rank, head_dim;
   float eps;
   int norm_rope;           // 0: plain pack, 1: full-width RMSNorm + RoPE, 2: per-head RMSNorm + RoPE
   int rope_style;          // 0: interleaved pairs (2j, 2j+1) over the head; 1: split half (j, j+rope_pairs)
   int rope_pairs;          // rotated pairs per head (head_dim/2 for style 0; a multiple of 8 for style 1)
   // Token-mode fan-out (kv_fanout > 0, world 1, heads_per_rank == heads): q rows go to q_out
-  // [seg_rows][heads][head_dim]; k and v rows go to each of dst[0..kv_fanout-1], blocks
-  // [2][seg_rows][heads][head_dim] (the all-gather of K/V as stores).
+  // [batch][seg_rows][heads][head_dim]; k and v rows go to each of dst[0..kv_fanout-1], blocks
+  // [2][batch][seg_rows][heads][head_dim] (the all-gather of K/V as stores).
   void* q_out;
   int kv_fanout;
 };
@@ -84,11 +86,13 @@ struct PrepassArgs {
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream);
 
 struct UnpackArgs {
-  const void* recv;        // head block src, row i at recv + src*src_stride + i*row_stride (elements)
-  int64_t src_stride, row_stride;
-  void* out;               // [n_local][heads][head_dim] (row stride below)
+  const void* recv;        // head block src, batch b, row i at recv + src*src_stride + b*batch_stride
+                           // + i*row_stride (elements)
+  int64_t src_stride, batch_stride, row_stride;
+  void* out;               // [batch][n_local][heads][head_dim] (strides below)
+  int64_t out_batch_stride;// elements between consecutive batch rows of out
   int64_t out_row_stride;  // elements between consecutive tokens of out
-  int world, n_local, seg_rows, heads, heads_per_rank, head_dim;
+  int batch, world, n_local, seg_rows, heads, heads_per_rank, head_dim;
   int out_fp32;            // 1: write fp32, 0: same 16-bit type as recv
 };
 

@@ -1,7 +1,8 @@
 // HBM-bound kernels around the attention: the fused q/k RMSNorm + RoPE +
 // Ulysses pack ("pre-pass") and the receive-side head->sequence unpack.
 //
-// Pre-pass, one CTA of 256 threads per token row of the send segment (seg_rows CTAs):
+// Pre-pass, one CTA of 256 threads per token row of the send segment and
+// batch row (a seg_rows x batch grid):
 //   q, k: y = bf16(fp32(x) * rsqrt(mean(x^2) + eps) * w)   (RMSNorm over the
 //         full width (Wan, norm_rope 1) or over each head (Flux / H3 QK-norm,
 //         norm_rope 2, weight [head_dim] shared by the heads))
@@ -10,7 +11,8 @@
 //         RoPE of H3, style 1; elements >= 2P keep y)
 //   v   : copied.
 // Each result goes straight to its slot of the all-to-all send buffer
-// [world][3][seg_rows][heads_per_rank][head_dim]: global head g lands in
+// [world][3][batch][seg_rows][heads_per_rank][head_dim] (the reference's
+// [W, T, B, width, h, D] packing): global head g lands in
 // destination block g / heads_per_rank at head slot g % heads_per_rank.
 // Rows past the local token count and heads past `heads` are written as
 // zeros (they are the zero padding of the reference's packing).
@@ -93,6 +95,7 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
   __shared__ float2 red[kThreads / 32];
   __shared__ uint16_t* sdst[kMaxSegs];
   const int i = blockIdx.x;
+  const int b = blockIdx.y;
   const int tid = threadIdx.x;
   if (tid < (a.kv_fanout > a.world ? a.kv_fanout : a.world)) sdst[tid] = static_cast<uint16_t*>(a.dst[tid]);
   __syncthreads();
@@ -100,8 +103,9 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
   const int h = a.heads_per_rank;
   const int vph = D >> 3;             // vectors per head
   const int nvec = a.heads * vph;     // vectors per token row
-  const int64_t block_elems = static_cast<int64_t>(a.seg_rows) * h * D;  // one [seg_rows][h][D] block
-  const int64_t row_off = static_cast<int64_t>(i) * h * D;
+  // One kind's [batch][seg_rows][h][D] block; this CTA's row within it.
+  const int64_t block_elems = static_cast<int64_t>(a.batch) * a.seg_rows * h * D;
+  const int64_t row_off = (static_cast<int64_t>(b) * a.seg_rows + i) * h * D;
   // Destination of vector (head g, element dd) of kind 0; kinds k add k*block_elems.
   auto slot0 = [&](int g, int dd) -> uint16_t* {
     const int dst = g / h;
@@ -146,7 +150,8 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
   uint4 xv[3][kVec];
 #pragma unroll
   for (int kind = 0; kind < 3; ++kind) {
-    const uint16_t* x = static_cast<const uint16_t*>(a.x[kind]) + static_cast<int64_t>(i) * a.x_row_stride[kind];
+    const uint16_t* x = static_cast<const uint16_t*>(a.x[kind]) + static_cast<int64_t>(b) * a.x_batch_stride[kind] +
+                        static_cast<int64_t>(i) * a.x_row_stride[kind];
 #pragma unroll
     for (int u = 0; u < kVec; ++u)
       if (live[u]) xv[kind][u] = __ldg(reinterpret_cast<const uint4*>(x + gv[u] * a.x_head_stride[kind] + ddv[u]));
@@ -202,7 +207,8 @@ __global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(co
           r[kind][u] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, static_cast<float>(D)), a.eps)));
         }
     }
-    const float* frow = a.freqs + static_cast<int64_t>(i) * a.freqs_row_stride;
+    const float* frow =
+        a.freqs + static_cast<int64_t>(b) * a.freqs_batch_stride + static_cast<int64_t>(i) * a.freqs_row_stride;
     constexpr bool split = kSplit;  // split-half partial RoPE (H3); else interleaved pairs
     const int half_vec = a.rope_pairs >> 3;  // split style: vectors between an element and its partner
     const int lane = tid & 31;
@@ -318,18 +324,22 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
   const int h = a.heads_per_rank;
   const int vph = D >> 3;
   const int per_token = a.heads * vph;
-  const int total = a.n_local * per_token;
+  const int per_batch = a.n_local * per_token;
+  const int total = a.batch * per_batch;
   for (int idx = blockIdx.x * kUnpackThreads + threadIdx.x; idx < total; idx += gridDim.x * kUnpackThreads) {
-    const int i = idx / per_token;
-    const int rem = idx - i * per_token;
+    const int b = idx / per_batch;
+    const int ib = idx - b * per_batch;
+    const int i = ib / per_token;
+    const int rem = ib - i * per_token;
     const int g = rem / vph;
     const int dd = (rem - g * vph) * 8;
     const int src = g / h;
     const int j = g - src * h;
-    const uint16_t* in = static_cast<const uint16_t*>(a.recv) + src * a.src_stride + i * a.row_stride +
-                         static_cast<int64_t>(j) * D + dd;
+    const uint16_t* in = static_cast<const uint16_t*>(a.recv) + src * a.src_stride + b * a.batch_stride +
+                         i * a.row_stride + static_cast<int64_t>(j) * D + dd;
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(in));
-    const int64_t o = static_cast<int64_t>(i) * a.out_row_stride + static_cast<int64_t>(g) * D + dd;
+    const int64_t o = static_cast<int64_t>(b) * a.out_batch_stride + static_cast<int64_t>(i) * a.out_row_stride +
+                      static_cast<int64_t>(g) * D + dd;
     if constexpr (kOutFp32) {
       uint16_t e[8];
       unpack8(v, e);
@@ -356,8 +366,8 @@ __global__ void __launch_bounds__(256) broadcast_kernel(const BroadcastArgs a) {
 
 int launch_prepass(const PrepassArgs& a, bool fp16, cudaStream_t stream) {
   using namespace pre;
-  if (a.seg_rows == 0) return 0;
-  const dim3 grid(a.seg_rows), block(kThreads);
+  if (a.seg_rows == 0 || a.batch == 0) return 0;
+  const dim3 grid(a.seg_rows, a.batch), block(kThreads);
   const int nvec = a.heads * (a.head_dim / 8);
   const int vec = (nvec + kThreads - 1) / kThreads;  // 1..kMaxVec (width <= 8192 is checked by the caller)
   const bool split = a.rope_style == 1 && a.norm_rope != 0;
@@ -405,7 +415,7 @@ int launch_broadcast(const BroadcastArgs& a, cudaStream_t stream) {
 
 int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream) {
   using namespace pre;
-  const int64_t total = static_cast<int64_t>(a.n_local) * a.heads * (a.head_dim / 8);
+  const int64_t total = static_cast<int64_t>(a.batch) * a.n_local * a.heads * (a.head_dim / 8);
   if (total == 0) return 0;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);

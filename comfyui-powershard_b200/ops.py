@@ -131,6 +131,13 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
     mode = int(norm_rope)
     lib = _lib.load()
     _check16(send, "prepass send")
+    if send.dim() == 6:  # batched send buffer [W, 3, B, width, h, D]
+        batch = send.shape[2]
+        if tuple(send.shape) != geo.send_shape(batch) or not send.is_contiguous():
+            raise ValueError(f"prepass: send must be contiguous {geo.send_shape(batch)}")
+        prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, send_blocks(send), geo, send.dtype, eps, norm_rope,
+                   rope_split_pairs, batch=batch)
+        return
     if tuple(send.shape) != geo.send_shape() or not send.is_contiguous():
         raise ValueError(f"prepass: send must be contiguous {geo.send_shape()}")
     args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, send.dtype, send.device, mode, rope_split_pairs)
@@ -142,19 +149,51 @@ def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo: UlyssesGeometry, eps: flo
 
 
 def prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, dst_blocks, geo: UlyssesGeometry, dtype: torch.dtype,
-               eps: float = 1e-6, norm_rope=True, rope_split_pairs=None):
+               eps: float = 1e-6, norm_rope=True, rope_split_pairs=None, batch: int | None = None):
     """``prepass`` storing destination d's [3,width,h,D] block at the device
-    address ``dst_blocks[d]`` (a peer's receive buffer: the fused exchange)."""
+    address ``dst_blocks[d]`` (a peer's receive buffer: the fused exchange).
+
+    With ``batch`` B the inputs carry a leading batch axis (x_* [B, n, H*D]
+    or [B, n, H, D], any batch stride; freqs [n, P, 2, 2] shared by the rows
+    or [B, n, P, 2, 2]) and each destination block is [3, B, width, h, D]."""
     mode = int(norm_rope)
     lib = _lib.load()
     if len(dst_blocks) != geo.world:
         raise ValueError(f"prepass_to: {len(dst_blocks)} destination blocks for {geo.world} ranks")
-    args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, dtype, x_q.device, mode, rope_split_pairs)
-    rc = lib.ps_b200_prepass_to(
-        *args, _lib.ptrs(dst_blocks), _lib.dtype_code(dtype),
-        geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
-        mode, *_rope_args(geo.head_dim, rope_split_pairs), _lib.stream_handle(x_q.device))
-    _lib.check(rc, "ps_b200_prepass_to")
+    if batch is None:
+        args = _prepass_inputs(x_q, x_k, x_v, w_q, w_k, freqs, geo, dtype, x_q.device, mode, rope_split_pairs)
+        rc = lib.ps_b200_prepass_to(
+            *args, _lib.ptrs(dst_blocks), _lib.dtype_code(dtype),
+            geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank, geo.head_dim, float(eps),
+            mode, *_rope_args(geo.head_dim, rope_split_pairs), _lib.stream_handle(x_q.device))
+        _lib.check(rc, "ps_b200_prepass_to")
+        return
+    batch = int(batch)
+    xs = (x_q, x_k, x_v)
+    for t, name in zip(xs, "qkv"):
+        if t.dim() not in (3, 4) or t.shape[0] != batch:
+            raise ValueError(f"prepass {name}: expected a leading batch axis of {batch}, got {tuple(t.shape)}")
+    # Row b of a batched input is x[b]: validate one row, pass the batch strides.
+    fb = 0
+    f_row = freqs
+    if mode and freqs is not None and freqs.dim() == 5:
+        if freqs.shape[0] != batch:
+            raise ValueError(f"prepass: batched freqs must have {batch} rows")
+        fb, f_row = freqs.stride(0), freqs[0]
+    args = _prepass_inputs(x_q[0], x_k[0], x_v[0], w_q, w_k, f_row, geo, dtype, x_q.device, mode, rope_split_pairs)
+    ptrs = [t.data_ptr() for t in xs]
+    rc = lib.ps_b200_prepass_batch(
+        *ptrs, _lib.i64([t.stride(0) for t in xs]), *args[3:9], fb, args[9], _lib.ptrs(dst_blocks),
+        _lib.dtype_code(dtype), batch, geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank,
+        geo.head_dim, float(eps), mode, *_rope_args(geo.head_dim, rope_split_pairs), _lib.stream_handle(x_q.device))
+    _lib.check(rc, "ps_b200_prepass_batch")
+
+
+def send_blocks(send: torch.Tensor):
+    """Device address of each destination's block of a local send buffer
+    (its slices along the leading world axis)."""
+    step = send[0].numel() * send.element_size()
+    return [send.data_ptr() + d * step for d in range(send.shape[0])]
 
 
 def attention_workspace(device: torch.device) -> torch.Tensor:
@@ -182,6 +221,14 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
     lib = _lib.load()
     _check16(recv, "attention recv")
     _lib.require_cuda(out_send, "attention out")
+    if recv.dim() == 6:  # batched [W, 3, B, width, h, D] -> out_send [W, B, width, h, D]
+        batch = recv.shape[2]
+        if tuple(out_send.shape) != geo.out_shape(batch) or not out_send.is_contiguous():
+            raise ValueError(f"attention: out must be contiguous {geo.out_shape(batch)}")
+        h, d = geo.heads_per_rank, geo.head_dim
+        ulysses_attention_to(recv, send_blocks(out_send), h * d, out_send.dtype, geo, scale, status, workspace,
+                             batch=batch, out_batch_stride=geo.width * h * d)
+        return
     if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
         raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")
     if tuple(out_send.shape) != geo.out_shape() or not out_send.is_contiguous():
@@ -234,6 +281,13 @@ def unpack(out_recv, out, geo: UlyssesGeometry):
     lib = _lib.load()
     _check16(out_recv, "unpack recv")
     _lib.require_cuda(out, "unpack out")
+    if out_recv.dim() == 5:  # batched [W, B, width, h, D] -> out [B, n, H, D]
+        batch = out_recv.shape[1]
+        if tuple(out_recv.shape) != geo.out_shape(batch) or not out_recv.is_contiguous():
+            raise ValueError(f"unpack: recv must be contiguous {geo.out_shape(batch)}")
+        h, d = geo.heads_per_rank, geo.head_dim
+        _unpack_batch(out_recv, batch * geo.width * h * d, geo.width * h * d, h * d, out, geo, batch)
+        return
     if tuple(out_recv.shape) != geo.out_shape() or not out_recv.is_contiguous():
         raise ValueError(f"unpack: recv must be contiguous {geo.out_shape()}")
     if (out.dim() != 3 or tuple(out.shape) != (geo.n_local, geo.heads, geo.head_dim)
@@ -247,12 +301,31 @@ def unpack(out_recv, out, geo: UlyssesGeometry):
 
 
 def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch.dtype, geo: UlyssesGeometry,
-                         scale: float, status: DeviceStatus | None, workspace=None):
+                         scale: float, status: DeviceStatus | None, workspace=None, batch: int | None = None,
+                         out_batch_stride: int = 0):
     """``ulysses_attention`` storing segment s's valid rows at the device
     address ``out_blocks[s]`` (row stride ``out_row_stride`` elements, head j
-    at + j*D): each source rank's staging buffer, the fused output exchange."""
+    at + j*D): each source rank's staging buffer, the fused output exchange.
+    With ``batch`` B, recv is [W, 3, B, width, h, D] and batch row b of
+    segment s starts at out_blocks[s] + b * out_batch_stride elements."""
     lib = _lib.load()
     _check16(recv, "attention recv")
+    if batch is not None:
+        if tuple(recv.shape) != geo.send_shape(batch) or not recv.is_contiguous():
+            raise ValueError(f"attention: recv must be contiguous {geo.send_shape(batch)}")
+        if len(out_blocks) != geo.world:
+            raise ValueError(f"attention: {len(out_blocks)} output blocks for {geo.world} ranks")
+        if out_dtype not in (recv.dtype, torch.float32):
+            raise ValueError("attention: output dtype must be fp32 or the input dtype")
+        rc = lib.ps_b200_ulysses_attn_batch(
+            recv.data_ptr(), _lib.ptrs(out_blocks), int(out_batch_stride), int(out_row_stride),
+            _lib.dtype_code(recv.dtype), _lib.dtype_code(out_dtype), int(batch), geo.world, geo.width, geo.total,
+            _seg_table(geo), geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale), *_ws(workspace),
+            status.ptr if status is not None else None, _lib.stream_handle(recv.device))
+        _lib.check(rc, "ps_b200_ulysses_attn_batch")
+        if status is not None:
+            status.arm()
+        return
     if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
         raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")
     if len(out_blocks) != geo.world:
@@ -310,12 +383,35 @@ def broadcast(dst_ptrs, src: torch.Tensor):
     _lib.check(rc, "ps_b200_broadcast")
 
 
+def _unpack_batch(src, src_stride: int, batch_stride: int, row_stride: int, out, geo: UlyssesGeometry, batch: int):
+    """Head blocks of ``src`` (block s, batch row b, token i at src + s*src_stride
+    + b*batch_stride + i*row_stride elements) -> out [B, n_local, H, D]."""
+    lib = _lib.load()
+    if (out.dim() != 4 or tuple(out.shape) != (batch, geo.n_local, geo.heads, geo.head_dim)
+            or out.stride(3) != 1 or out.stride(2) != geo.head_dim):
+        raise ValueError(f"unpack: out must be [{batch}, {geo.n_local}, {geo.heads}, {geo.head_dim}] "
+                         "with packed heads")
+    rc = lib.ps_b200_unpack_batch(
+        src.data_ptr(), int(src_stride), int(batch_stride), int(row_stride), out.data_ptr(), out.stride(0),
+        out.stride(1), _lib.dtype_code(src.dtype), _lib.dtype_code(out.dtype), int(batch), geo.n_local, geo.heads,
+        geo.heads_per_rank, geo.head_dim, _lib.stream_handle(out.device))
+    _lib.check(rc, "ps_b200_unpack_batch")
+
+
 def unpack_staged(staging, out, geo: UlyssesGeometry):
     """Staging buffer [width, W*h, D] (rows of this rank, every head block) ->
     out [n_local, H, D] (real heads only)."""
     lib = _lib.load()
     _check16(staging, "unpack staging")
     _lib.require_cuda(out, "unpack out")
+    if staging.dim() == 4:  # batched [B, width, W*h, D] -> out [B, n, H, D]
+        batch = staging.shape[0]
+        shape = (batch, geo.width, geo.padded_heads, geo.head_dim)
+        if tuple(staging.shape) != shape or not staging.is_contiguous():
+            raise ValueError(f"unpack: staging must be contiguous {shape}")
+        h, d = geo.heads_per_rank, geo.head_dim
+        _unpack_batch(staging, h * d, geo.width * geo.padded_heads * d, geo.padded_heads * d, out, geo, batch)
+        return
     shape = (geo.width, geo.padded_heads, geo.head_dim)
     if tuple(staging.shape) != shape or not staging.is_contiguous():
         raise ValueError(f"unpack: staging must be contiguous {shape}")

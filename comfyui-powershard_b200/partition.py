@@ -122,18 +122,26 @@ class UlyssesGeometry:
         all W head blocks: rank 0 of a rows*W sequence has exactly those rows."""
         return cls(total=rows * world, heads=heads, head_dim=head_dim, world=world, rank=0)
 
-    def send_shape(self):
-        return (self.world, 3, self.width, self.heads_per_rank, self.head_dim)
+    def send_shape(self, batch: int | None = None):
+        """[W, 3, width, h, D], or with a batch axis [W, 3, B, width, h, D]
+        (the reference's packing, powershard/wan_model.py:356-361)."""
+        if batch is None:
+            return (self.world, 3, self.width, self.heads_per_rank, self.head_dim)
+        return (self.world, 3, int(batch), self.width, self.heads_per_rank, self.head_dim)
 
-    def out_shape(self):
-        return (self.world, self.width, self.heads_per_rank, self.head_dim)
+    def out_shape(self, batch: int | None = None):
+        """[W, width, h, D], or [W, B, width, h, D] (wan_model.py:373-376)."""
+        if batch is None:
+            return (self.world, self.width, self.heads_per_rank, self.head_dim)
+        return (self.world, int(batch), self.width, self.heads_per_rank, self.head_dim)
 
-    def exchanged_bytes(self, element_size: int) -> tuple[int, int]:
-        """Bytes of the QKV send buffer and of the output send buffer."""
+    def exchanged_bytes(self, element_size: int, batch: int = 1) -> tuple[int, int]:
+        """Bytes of the QKV send buffer and of the output send buffer of one
+        call (the reference's send.numel() * element_size, wan_model.py:364, 381)."""
         n = 1
-        for s in self.send_shape():
+        for s in self.send_shape(batch):
             n *= s
         m = 1
-        for s in self.out_shape():
+        for s in self.out_shape(batch):
             m *= s
         return n * element_size, m * element_size

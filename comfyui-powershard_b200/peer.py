@@ -5,11 +5,11 @@ The reference moves q/k/v and the attention output with two
 Here each rank instead owns two buffers that every rank of the group maps
 into its address space (CUDA IPC):
 
-* ``recv``    [W][3][width][h][D]: rank s's pre-pass stores its block for
-  this rank at ``recv[s]`` directly over NVLink (``ps_b200_prepass_to``);
-* ``staging`` [width][W*h][D]: the attention kernel of rank r stores the
+* ``recv``    [W][3][B][width][h][D]: rank s's pre-pass stores its block for
+  this rank at ``recv[s]`` directly over NVLink (``ps_b200_prepass_batch``);
+* ``staging`` [B][width][W*h][D]: the attention kernel of rank r stores the
   output rows of this rank's tokens for heads [r*h, (r+1)*h) directly into
-  ``staging[:, r*h:(r+1)*h]`` (``ps_b200_ulysses_attn_to``);
+  ``staging[:, :, r*h:(r+1)*h]`` (``ps_b200_ulysses_attn_batch``);
 * ``text`` [W][P][h][D] (joint attention only): rank r copies the text
   outputs of its heads into ``text[r]`` of every rank (``ps_b200_broadcast``),
   the all-gather over heads of the replicated text rows;
@@ -65,10 +65,11 @@ class PeerExchange:
     """
 
     def __init__(self, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
-                 layout: str = "ulysses"):
+                 layout: str = "ulysses", batch: int | None = None):
         self.group, self.geo, self.dtype, self.device = group, geo, dtype, device
         self.text_rows = int(text_rows)
         self.layout = layout
+        self.batch = batch  # None: unbatched buffers [W][3][width][h][D] / [width][W*h][D]
         self.own = []         # device pointers this rank allocated
         self.imported = []    # device pointers mapped from peers
         self.recv_ptrs = []
@@ -79,8 +80,8 @@ class PeerExchange:
     # ------------------------------------------------------------ setup
     @classmethod
     def create(cls, group, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
-               layout: str = "ulysses"):
-        ex = cls(group, geo, dtype, device, text_rows, layout)
+               layout: str = "ulysses", batch: int | None = None):
+        ex = cls(group, geo, dtype, device, text_rows, layout, batch)
         ok, reason = ex._setup()
         verdict = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
         dist.all_reduce(verdict, op=dist.ReduceOp.MIN, group=group)
@@ -96,6 +97,8 @@ class PeerExchange:
         h, d = geo.heads_per_rank, geo.head_dim
         if self.layout == "token":  # gathered K/V of every rank: [W][2][width][H][D]
             shapes = [(geo.world, 2, geo.width, geo.heads, d)]
+        elif self.batch is not None:
+            shapes = [geo.send_shape(self.batch), (self.batch, geo.width, geo.padded_heads, d)]
         else:
             shapes = [geo.send_shape(), (geo.width, geo.padded_heads, d)]
             if self.text_rows:
@@ -145,10 +148,12 @@ class PeerExchange:
         self.recv_ptrs, self.stage_ptrs = ptrs[0], ptrs[1]
         self.recv = _wrap(self.own[0], shapes[0], self.dtype, self.device)
         self.staging = _wrap(self.own[1], shapes[1], self.dtype, self.device)
-        block = 3 * geo.width * h * d * esize                   # one source's [3][width][h][D] block
+        nb = 1 if self.batch is None else self.batch
+        block = 3 * nb * geo.width * h * d * esize              # one source's [3][B][width][h][D] block
         self.dst_blocks = [p + geo.rank * block for p in self.recv_ptrs]
         self.out_blocks = [p + geo.rank * h * d * esize for p in self.stage_ptrs]
         self.out_row_stride = geo.padded_heads * d
+        self.out_batch_stride = geo.width * geo.padded_heads * d
         if self.text_rows:
             self.text = _wrap(self.own[2], shapes[2], self.dtype, self.device)
             tblock = self.text_rows * h * d * esize

@@ -18,10 +18,12 @@ destination's block straight into that rank's receive buffer, the attention
 epilogue stores each output row straight into its owner's staging buffer,
 and two 4-byte all-reduces order the steps across ranks (``peer.py``).
 
-This replaces, for one batch row, powershard/wan_model.py:421-430
-(attention_qkv) + 343-364 (ulysses_to_sequence) + 398-418 (run_attention) +
-367-381 (ulysses_to_heads).  Buffers are cached per (device, stream,
-geometry, dtype) and reused; the returned output is always a fresh tensor.
+This replaces powershard/wan_model.py:421-430 (attention_qkv) + 343-364
+(ulysses_to_sequence) + 398-418 (run_attention) + 367-381
+(ulysses_to_heads) for a whole batch (e.g. the CFG pair) in one exchange,
+with the reference's batched packing [W][3][B][width][h][D].  Buffers are
+cached per (device, stream, geometry, batch, dtype) and reused; the
+returned output is always a fresh tensor.
 """
 from __future__ import annotations
 
@@ -61,6 +63,7 @@ class UlyssesAttention:
         self._status = {}
         self._peers = {}
         self._attn_ws = {}
+        self.last_exchange = None  # exchange the last token-mode call used
 
     # ------------------------------------------------------------ topology
     def world_rank(self):
@@ -77,14 +80,14 @@ class UlyssesAttention:
                                sizes=None if sizes is None else tuple(sizes))
 
     # ------------------------------------------------------------ buffers
-    def _workspace(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device):
+    def _workspace(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, batch: int | None = None):
         stream = torch.cuda.current_stream(device).cuda_stream if device.type == "cuda" else 0
-        key = (device.index, stream, geo.world, geo.width, geo.heads_per_rank, geo.head_dim, dtype)
+        key = (device.index, stream, geo.world, geo.width, geo.heads_per_rank, geo.head_dim, dtype, batch)
         ws = self._buffers.get(key)
         if ws is None:
-            send = torch.empty(geo.send_shape(), dtype=dtype, device=device)
+            send = torch.empty(geo.send_shape(batch), dtype=dtype, device=device)
             recv = send if geo.world == 1 else torch.empty_like(send)
-            out_send = None if geo.world == 1 else torch.empty(geo.out_shape(), dtype=dtype, device=device)
+            out_send = None if geo.world == 1 else torch.empty(geo.out_shape(batch), dtype=dtype, device=device)
             out_recv = None if geo.world == 1 else torch.empty_like(out_send)
             ws = dict(send=send, recv=recv, out_send=out_send, out_recv=out_recv)
             self._buffers[key] = ws
@@ -95,7 +98,7 @@ class UlyssesAttention:
             dist.all_to_all_single(recv, send, group=self.group)
 
     def _peer(self, geo: UlyssesGeometry, dtype: torch.dtype, device: torch.device, text_rows: int = 0,
-              layout: str = "ulysses"):
+              layout: str = "ulysses", batch: int | None = None):
         """The peer exchange of this geometry, or None for the NCCL path."""
         if geo.world == 1 or self.exchange == "nccl" or self.kernels is not ops or device.type != "cuda":
             return None
@@ -103,10 +106,10 @@ class UlyssesAttention:
             return None
         stream = torch.cuda.current_stream(device).cuda_stream
         key = (layout, device.index, stream, geo.world, geo.rank, geo.width, geo.heads, geo.head_dim, dtype,
-               text_rows)
+               text_rows, batch)
         if key not in self._peers:
             from .peer import PeerExchange
-            ex = PeerExchange.create(self.group, geo, dtype, device, text_rows, layout)
+            ex = PeerExchange.create(self.group, geo, dtype, device, text_rows, layout, batch)
             if ex is None and self.exchange == "peer":
                 raise RuntimeError("peer exchange requested but the ranks cannot map each other's memory")
             self._peers[key] = ex
@@ -124,54 +127,79 @@ class UlyssesAttention:
                 eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
                 norm_rope: bool = True, state: dict | None = None, local: bool = False,
                 rope_split_pairs: int | None = None) -> torch.Tensor:
-        """One block's self-attention for this rank's tokens.
+        """One block's self-attention for this rank's tokens (one batch row).
 
-        x_q/x_k/x_v: [n_local, H*D] q/k/v projection outputs (bf16/fp16).
-        With norm_rope, w_q/w_k [H*D] are the RMSNorm weights and freqs is
-        the rank's rotation table [n_local, D/2, 2, 2] fp32; without it the
-        inputs are already normalised/rotated and are only exchanged.
-        norm_rope may also be ops.NORM_PER_HEAD (w_q/w_k [D]); rope_split_pairs
-        P selects the split-half partial RoPE of H3 (freqs [n_local, P, 2, 2]).
-        Returns [n_local, H, D] in out_dtype (default: the input dtype).
-        local=True runs the block on this rank alone (no exchange, W = 1).
+        x_q/x_k/x_v: [n_local, H*D] (or [n_local, H, D]) q/k/v projection
+        outputs (bf16/fp16).  With norm_rope, w_q/w_k [H*D] are the RMSNorm
+        weights and freqs is the rank's rotation table [n_local, D/2, 2, 2]
+        fp32; without it the inputs are already normalised/rotated and are
+        only exchanged.  norm_rope may also be ops.NORM_PER_HEAD (w_q/w_k
+        [D]); rope_split_pairs P selects the split-half partial RoPE of H3
+        (freqs [n_local, P, 2, 2]).  Returns [n_local, H, D] in out_dtype
+        (default: the input dtype).  local=True runs the block on this rank
+        alone (no exchange, W = 1).  ``forward_batch`` is the same for a
+        batch of rows in one exchange.
+        """
+        return self.forward_batch(x_q[None], x_k[None], x_v[None], w_q, w_k, freqs, total=total, heads=heads,
+                                  eps=eps, scale=scale, out_dtype=out_dtype, norm_rope=norm_rope, state=state,
+                                  local=local, rope_split_pairs=rope_split_pairs)[0]
+
+    def forward_batch(self, x_q, x_k, x_v, w_q=None, w_k=None, freqs=None, *, total: int, heads: int,
+                      eps: float = 1e-6, scale: float | None = None, out_dtype: torch.dtype | None = None,
+                      norm_rope: bool = True, state: dict | None = None, local: bool = False,
+                      rope_split_pairs: int | None = None) -> torch.Tensor:
+        """``forward`` for B batch rows in one exchange, as the reference
+        moves a whole batch with one all_to_all_single each way
+        (powershard/wan_model.py:356-362, :373-378).
+
+        x_*: [B, n_local, H*D] or [B, n_local, H, D] (any batch/row/head
+        strides, unit inner stride); freqs [n_local, P, 2, 2] shared by the
+        rows, or [B, n_local, P, 2, 2].  Returns [B, n_local, H, D].  One
+        pre-pass, one attention launch and one unpack serve the whole batch;
+        the state counters count the batch's bytes once.
         """
         device = x_q.device
         dtype = x_q.dtype
-        head_dim = x_q.shape[-1] if x_q.dim() == 3 else x_q.shape[-1] // heads
+        batch = x_q.shape[0]
+        head_dim = x_q.shape[-1] if x_q.dim() == 4 else x_q.shape[-1] // heads
         geo = self.geometry(total, heads, head_dim, local)
-        if x_q.shape[0] != geo.n_local:
+        if x_q.shape[1] != geo.n_local:
             raise ValueError("Ulysses local token/head geometry mismatch")
         out_dtype = out_dtype or dtype
         scale = head_dim ** -0.5 if scale is None else float(scale)
         k = self.kernels
+        h, d = geo.heads_per_rank, head_dim
         with torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext():
-            px = self._peer(geo, dtype, device)
+            out = torch.empty((batch, geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
+            if batch == 0:
+                return out
+            px = self._peer(geo, dtype, device, batch=batch)
             if px is not None:
                 status = self._device_status(device)
                 status.poll()
-                out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
                 k.prepass_to(x_q, x_k, x_v, w_q, w_k, freqs, px.dst_blocks, geo, dtype, eps, norm_rope,
-                             **self._rope_kw(rope_split_pairs))
+                             **self._rope_kw(rope_split_pairs), batch=batch)
                 px.barrier()
                 k.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status,
-                                       **self._ws(device))
+                                       **self._ws(device), batch=batch, out_batch_stride=px.out_batch_stride)
                 px.barrier()
                 k.unpack_staged(px.staging, out, geo)
-                self._count(state, geo, dtype, "peer")
+                self._count(state, geo, dtype, "peer", batch)
                 return out
-            ws, status = self._workspace(geo, dtype, device)
+            ws, status = self._workspace(geo, dtype, device, batch)
             status.poll()
-            out = torch.empty((geo.n_local, heads, head_dim), dtype=out_dtype, device=device)
             k.prepass(x_q, x_k, x_v, w_q, w_k, freqs, ws["send"], geo, eps, norm_rope,
                       **self._rope_kw(rope_split_pairs))
             self._exchange(ws["recv"], ws["send"], geo)
             if geo.world == 1:
-                k.ulysses_attention(ws["recv"], out.view(geo.out_shape()), geo, scale, status, **self._ws(device))
+                # The final [B, n, H, D] output is the only segment's output block.
+                k.ulysses_attention(ws["recv"], out.view(1, batch, geo.n_local, heads, head_dim), geo, scale,
+                                    status, **self._ws(device))
             else:
                 k.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status, **self._ws(device))
                 self._exchange(ws["out_recv"], ws["out_send"], geo)
                 k.unpack(ws["out_recv"], out, geo)
-        self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local")
+        self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local", batch)
         return out
 
     def _ws(self, device) -> dict:
@@ -194,12 +222,13 @@ class UlyssesAttention:
         return self._status[device.index]
 
     @staticmethod
-    def _count(state, geo, dtype, exchange):
+    def _count(state, geo, dtype, exchange, batch=1):
         """The reference's sequence-state counters (powershard/wan_model.py:441-502):
-        one q/k/v exchange and one output exchange per block, with their bytes."""
+        one q/k/v exchange and one output exchange per block, with the bytes
+        of the whole batch's send buffers (wan_model.py:364, :381)."""
         if state is None:
             return
-        qkv_bytes, out_bytes = geo.exchanged_bytes(dtype.itemsize)
+        qkv_bytes, out_bytes = geo.exchanged_bytes(dtype.itemsize, batch)
         state["padded_heads"] = geo.padded_heads
         state["kv_collectives"] = state.get("kv_collectives", 0) + 1
         state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + qkv_bytes
@@ -278,13 +307,19 @@ class UlyssesAttention:
         self._count_token(state, total, heads, head_dim, dtype, "nccl" if world > 1 else "local")
         return out
 
+    def _count_token(self, state, total, heads, head_dim, dtype, exchange, batch=1):
+        self.last_exchange = exchange
+        self.count_token(state, total, heads, head_dim, dtype, exchange, batch)
+
     @staticmethod
-    def _count_token(state, total, heads, head_dim, dtype, exchange):
-        """Token-mode counters (wan_model.py:489-500): one K/V gather per block."""
+    def count_token(state, total, heads, head_dim, dtype, exchange, batch=1):
+        """Token-mode counters (wan_model.py:489-500): one K/V gather per block,
+        the gathered [B, total, 2, H, D] bytes."""
         if state is None:
             return
         state["kv_collectives"] = state.get("kv_collectives", 0) + 1
-        state["kv_gathered_bytes"] = state.get("kv_gathered_bytes", 0) + 2 * total * heads * head_dim * dtype.itemsize
+        state["kv_gathered_bytes"] = (state.get("kv_gathered_bytes", 0)
+                                      + 2 * batch * total * heads * head_dim * dtype.itemsize)
         state["effective_comm_dtype"] = str(dtype).replace("torch.", "")
         state["exchange"] = exchange
 

@@ -57,25 +57,49 @@ def _check_supported(module, state):
 
 
 def _rows(t, heads, head_dim, dtype):
-    """[n, H, D] or [n, H*D] -> contiguous [n, H*D] in the wire dtype."""
-    t = t.reshape(t.shape[0], heads * head_dim)
+    """[B, n, H, D] or [B, n, H*D] -> [B, n, H*D] in the wire dtype with unit
+    inner stride and 16-byte aligned rows (a copy only when needed)."""
+    t = t.reshape(t.shape[0], t.shape[1], heads * head_dim)
     if t.dtype != dtype:
         t = t.to(dtype)
-    if t.stride(1) != 1 or t.stride(0) % 8 or t.data_ptr() % 16:
+    if t.stride(-1) != 1 or any(st % 8 for st in t.stride()[:-1]) or t.data_ptr() % 16:
         t = t.contiguous()
     return t
 
 
+def _run(engine, state, q, k, v, w_q, w_k, table, total, heads, norm_rope, out_dtype, local, eps=1e-6):
+    """The batch [B, n, H*D] through Ulysses (one exchange for the whole batch)
+    or token mode (the shared state's ``ulysses`` flag); counters once per call."""
+    token = state.get("enabled") and not state.get("ulysses", True)
+    counted = state if state.get("enabled") else None
+    if not token:
+        return engine.forward_batch(q, k, v, w_q, w_k, table, total=total, heads=heads, eps=eps,
+                                    norm_rope=norm_rope, out_dtype=out_dtype, state=counted, local=local)
+    outs = [engine.forward_token(q[b], k[b], v[b], w_q, w_k,
+                                 table[b] if table is not None and table.dim() == 5 else table,
+                                 total=total, heads=heads, eps=eps, norm_rope=norm_rope, out_dtype=out_dtype)
+            for b in range(q.shape[0])]
+    if counted is not None:
+        # The reference gathers the whole batch's K/V in one all-gather
+        # (wan_model.py:489-493): one collective, the batch's bytes.
+        engine.count_token(counted, total, heads, q.shape[-1] // heads, q.dtype, engine.last_exchange,
+                           batch=q.shape[0])
+    return torch.stack(outs)
+
+
 def self_attention_forward(self, x, freqs, transformer_options=None):
-    """x [B, n, dim] -> [B, n, dim] through the fused Ulysses path."""
+    """x [B, n, dim] -> [B, n, dim] through the fused Ulysses path (the whole
+    batch in one exchange, as the reference)."""
     state = _state(self)
     _check_supported(self, state)
     batch, n, _ = x.shape
     heads, dim = self.num_heads, self.head_dim
     total = state["total"] if state.get("enabled") else n
     engine = _engine(self)
-    table = freqs[0, :, 0]
-    if table.dtype != torch.float32 or table.stride()[1:] != (4, 2, 1) or table.data_ptr() % 16:
+    # The reference's table [1 or B, n, 1, D/2, 2, 2] (wan_model.py:325-329):
+    # one table shared by the batch rows, or one per row.
+    table = freqs[:, :, 0] if freqs.shape[0] > 1 else freqs[0, :, 0]
+    if table.dtype != torch.float32 or table.stride()[-3:] != (4, 2, 1) or table.data_ptr() % 16:
         table = table.float().contiguous()
     w_q = self.norm_q.weight
     w_k = self.norm_k.weight
@@ -83,17 +107,9 @@ def self_attention_forward(self, x, freqs, transformer_options=None):
         w_q, w_k = w_q.float(), w_k.float()
     eps = self.norm_q.eps if self.norm_q.eps is not None else 1e-6
     q_lin, k_lin, v_lin = self.q(x), self.k(x), self.v(x)
-    token = state.get("enabled") and not state.get("ulysses", True)
-    outs = []
-    for b in range(batch):
-        run = engine.forward_token if token else engine.forward
-        extra = {} if token else {"local": not state.get("enabled")}
-        outs.append(run(
-            _rows(q_lin[b], heads, dim, WIRE_DTYPE), _rows(k_lin[b], heads, dim, WIRE_DTYPE),
-            _rows(v_lin[b], heads, dim, WIRE_DTYPE), w_q.contiguous(), w_k.contiguous(), table,
-            total=total, heads=heads, eps=eps, norm_rope=True,
-            state=state if (b == 0 and state.get("enabled")) else None, **extra))
-    out = torch.stack(outs)
+    out = _run(engine, state, _rows(q_lin, heads, dim, WIRE_DTYPE), _rows(k_lin, heads, dim, WIRE_DTYPE),
+               _rows(v_lin, heads, dim, WIRE_DTYPE), w_q.contiguous(), w_k.contiguous(), table, total, heads,
+               True, None, not state.get("enabled"), eps)
     return self.o(out.reshape(batch, n, heads * dim).to(x.dtype if x.is_floating_point() else out.dtype))
 
 
@@ -111,14 +127,8 @@ def sequence_attention(self, q, k, v, total=None):
         return out.float()
     total = total or state["total"]
     engine = _engine(self)
-    run = engine.forward if state.get("ulysses", True) else engine.forward_token
-    outs = []
-    for b in range(batch):
-        outs.append(run(
-            _rows(q[b], heads, dim, WIRE_DTYPE), _rows(k[b], heads, dim, WIRE_DTYPE),
-            _rows(v[b], heads, dim, WIRE_DTYPE), total=total, heads=heads, norm_rope=False,
-            out_dtype=torch.float32, state=state if b == 0 else None))
-    return torch.stack(outs)
+    return _run(engine, state, _rows(q, heads, dim, WIRE_DTYPE), _rows(k, heads, dim, WIRE_DTYPE),
+                _rows(v, heads, dim, WIRE_DTYPE), None, None, None, total, heads, False, torch.float32, False)
 
 
 def gather_tokens(x, total, dtype=None, group=None):

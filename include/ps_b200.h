@@ -43,6 +43,11 @@
  *                          all-gather; the broadcast all-gathers text outputs.
  *   ps_b200_prepass rope_style 1   rope_split_half of the H3 path,
  *                          powershard/attention.py:98-103.
+ *   ps_b200_prepass_batch, ps_b200_ulysses_attn_batch, ps_b200_unpack_batch
+ *                          the same three steps for a batch of rows (CFG) in
+ *                          one exchange, as the reference packs it: send
+ *                          [W, T, B, width, h, D] (wan_model.py:350-362) and
+ *                          output send [W, B, width, h, D] (:373-378).
  *   ps_b200_kernel_launches, ps_b200_selftest_bounded_wait,
  *   ps_b200_block_fwd_static  no reference counterpart (instrumentation,
  *                          failure-detection self-test, allocation-free block).
@@ -62,7 +67,7 @@
 extern "C" {
 #endif
 
-#define PS_B200_ABI_VERSION 3
+#define PS_B200_ABI_VERSION 4
 
 /* Return codes. */
 #define PS_B200_OK 0
@@ -289,6 +294,52 @@ int ps_b200_ulysses_attn_to(const void* recv, void* const* out_blocks, int64_t o
                             int out_dtype, int world, int seg_rows, int total, const int* seg_valid,
                             int heads_per_rank, int heads_valid, int head_dim, float softmax_scale, void* workspace,
                             size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * Batched Ulysses steps: B rows of a batch (e.g. the CFG pair) go through one
+ * exchange, in the reference's packing (powershard/wan_model.py:350-362 and
+ * :373-378).  The existing entry points are the case batch = 1.
+ *
+ * ps_b200_prepass_batch: as ps_b200_prepass_to for rows b = 0..batch-1.  Row
+ *   (b, i) of x_* starts at x_* + b*x_batch_strides[.] + i*x_row_strides[.]
+ *   elements; its rotation table at freqs + b*freqs_batch_stride +
+ *   i*freqs_row_stride floats (freqs_batch_stride 0: one table for every
+ *   row).  dst_blocks[d] receives destination d's block
+ *   [3][batch][seg_rows][heads_per_rank][head_dim] (a slice of the local send
+ *   buffer [world][3][batch][seg_rows][h][D], or a peer's receive buffer).
+ */
+int ps_b200_prepass_batch(const void* x_q, const void* x_k, const void* x_v, const int64_t x_batch_strides[3],
+                          const int64_t x_row_strides[3], const int64_t x_head_strides[3], const void* w_qnorm,
+                          const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_batch_stride,
+                          int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int batch, int world,
+                          int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, float eps,
+                          int norm_rope, int rope_style, int rope_pairs, void* stream);
+
+/*
+ * ps_b200_ulysses_attn_batch: attention over the batched receive buffer recv
+ *   [world][3][batch][seg_rows][heads_per_rank][head_dim]; valid row i of
+ *   segment s, batch row b, head j goes to out_blocks[s] + b*out_batch_stride
+ *   + i*out_row_stride + j*head_dim elements (out_dtype): the batched output
+ *   send buffer [world][batch][seg_rows][h][D] (out_blocks[s] = its slice s,
+ *   batch stride seg_rows*h*D, row stride h*D), the owners' staging buffers
+ *   [batch][seg_rows][world*h][D] of the peer exchange, or at world 1 the
+ *   final [batch][n][heads][head_dim] output.
+ */
+int ps_b200_ulysses_attn_batch(const void* recv, void* const* out_blocks, int64_t out_batch_stride,
+                               int64_t out_row_stride, int dtype, int out_dtype, int batch, int world, int seg_rows,
+                               int total, const int* seg_valid, int heads_per_rank, int heads_valid, int head_dim,
+                               float softmax_scale, void* workspace, size_t workspace_bytes, int* status,
+                               void* stream);
+
+/*
+ * ps_b200_unpack_batch: as ps_b200_unpack_strided for batch rows; row i of
+ *   batch row b, head block src at recv + src*src_stride + b*batch_stride +
+ *   i*row_stride elements, written to out + b*out_batch_stride +
+ *   i*out_row_stride (+ head*head_dim).
+ */
+int ps_b200_unpack_batch(const void* recv, int64_t src_stride, int64_t batch_stride, int64_t row_stride, void* out,
+                         int64_t out_batch_stride, int64_t out_row_stride, int dtype, int out_dtype, int batch,
+                         int n_local, int heads, int heads_per_rank, int head_dim, void* stream);
 
 /*
  * Self-test of the bounded waits (no counterpart in the reference): one warp

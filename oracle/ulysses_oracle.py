@@ -35,7 +35,7 @@ __all__ = [
     "pack_out", "unpack_out", "math_attention", "sdpa_fp32", "sequence_attention", "gather_rows",
     "token_sequence_attention",
     "rms_norm_heads", "flux_joint_attention", "split_sizes", "image_local_ranges",
-    "image_sequence_attention", "time_reference_sample",
+    "image_sequence_attention", "time_reference_sample", "time_reference_step",
 ]
 
 
@@ -268,7 +268,7 @@ def _power2_scale(ratio: torch.Tensor) -> torch.Tensor:
 
 def sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: int,
                        eps: float = 1e-6, wire_dtype=torch.bfloat16, attention="sdpa",
-                       scale=None, provider_dtype=None):
+                       scale=None, provider_dtype=None, v_scales=None):
     """Whole Ulysses self-attention of one block, all ranks simulated in-process.
 
     Inputs are the GLOBAL projection outputs [1, L, H*D] and the global RoPE
@@ -282,7 +282,11 @@ def sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: in
 
     provider_dtype reproduces run_attention (wan_model.py:398-418): q/k are
     cast to that dtype, v divided by its power-of-two scale sv before the
-    cast, the provider output rounded to it and multiplied back by sv.
+    cast, the provider output rounded to it and multiplied back by sv.  The
+    reference takes sv over everything one call receives (v_scale,
+    wan_model.py:389-395), so a batch of rows shares it: ``v_scales`` (one
+    scalar tensor per rank) supplies that shared scale when this function
+    is called one batch row at a time.
     """
     total = q_lin.shape[1]
     sends = []
@@ -300,7 +304,10 @@ def sequence_attention(q_lin, k_lin, v_lin, wq, wk, freqs, heads: int, world: in
         if provider_dtype is None:
             o = fn(q[None].float(), k[None].float(), v[None].float(), scale)[0]
         else:
-            sv = _power2_scale(v.float().abs().amax() / 16384.0) if v.numel() else torch.ones(())
+            if v_scales is not None:
+                sv = v_scales[r]
+            else:
+                sv = _power2_scale(v.float().abs().amax() / 16384.0) if v.numel() else torch.ones(())
             o = fn(q[None].float().to(provider_dtype), k[None].float().to(provider_dtype),
                    (v[None].float() / sv).to(provider_dtype), scale)[0]
             o = o.to(provider_dtype).float() * sv
@@ -493,3 +500,53 @@ def time_reference_sample(total: int, heads: int, dim: int, budget_s: float = 12
                 prepass_s=prepass_s, attention_sample_s=attn_sample_s,
                 attention_chunks=done_chunks, attention_chunks_total=all_chunks,
                 threads=torch.get_num_threads())
+
+
+def time_reference_step(total: int, heads: int, dim: int, budget_s: float = 5.0,
+                        threads: int | None = None, seed: int = 0):
+    """One measured step of the reference's CPU algorithm on a bounded,
+    proportional slice of one layer (nothing extrapolated inside the step).
+
+    The step runs ``math_attention`` (128x512 fp32 tiles, the reference's
+    default provider, powershard/attention_contract.py:85-125) for query
+    chunks of 128 rows of one head against all ``total`` keys until
+    ``budget_s`` is spent - c chunks, the fraction f = c / (ceil(L/128)*H) of
+    the layer's attention - and then the per-token pre-pass (attention_qkv +
+    pack, powershard/wan_model.py:421-430 and 343-361) over the same fraction
+    f of the tokens.  Both parts scale linearly with f, so the step's rate
+    (attention FLOPs executed / wall time of the step) is the layer's rate.
+
+    Returns the step's wall seconds, the FLOPs it executed (4*128*c*L*D),
+    their rate, the chunks and tokens processed and the threads used.
+    """
+    if threads:
+        torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    width = heads * dim
+    all_chunks = math.ceil(total / 128) * heads
+    kk = torch.randn(1, total, 1, dim, generator=g)
+    vv = torch.randn(1, total, 1, dim, generator=g)
+    queries = [torch.randn(1, 128, 1, dim, generator=g) for _ in range(4)]
+    t0 = time.perf_counter()
+    chunks = 0
+    while True:
+        math_attention(queries[chunks % 4], kk, vv)
+        chunks += 1
+        if time.perf_counter() - t0 > budget_s or chunks >= all_chunks:
+            break
+    attn_s = time.perf_counter() - t0
+    tokens = max(1, round(total * chunks / all_chunks))
+    xs = [torch.randn(1, tokens, width, generator=g) for _ in range(3)]
+    ang = torch.rand(1, tokens, 1, dim // 2, generator=g) * 40.0
+    c, s = torch.cos(ang), torch.sin(ang)
+    freqs = torch.stack([c, -s, s, c], -1).reshape(1, tokens, 1, dim // 2, 2, 2)
+    w = torch.ones(width)
+    t1 = time.perf_counter()
+    q, k, v = attention_qkv(xs[0], xs[1], xs[2], w, w, freqs, heads)
+    pack_qkv(q[0], k[0], v[0], tokens, 0, 1)
+    prepass_s = time.perf_counter() - t1
+    wall = attn_s + prepass_s
+    flops = 4.0 * 128 * chunks * total * dim
+    return dict(wall_s=wall, flops=flops, tflops=flops / wall / 1e12, attention_s=attn_s,
+                prepass_s=prepass_s, chunks=chunks, chunks_total=all_chunks, tokens=tokens,
+                fraction=chunks / all_chunks, threads=torch.get_num_threads())

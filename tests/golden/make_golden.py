@@ -20,6 +20,10 @@ inputs + outputs with torch.save next to this script:
 * ``sequence_attention.pt`` - wan_model.sequence_attention (Ulysses, math
   provider, fp32 wire) for W in {1,2,3} on a 40-token, 5-head, D=128 layer;
   ``sequence_attention_token.pt`` the same in token mode (K/V all-gather).
+* ``self_attention_forward.pt`` - wan_model.self_attention_forward (q/k/v/o
+  operations.Linear + RMSNorm, attention_qkv, sequence_attention, o) on a
+  CFG batch of 2 rows, W=1 (sequence state off, math provider) and Ulysses
+  W=2 (math provider, fp32 wire), with the state counters of each rank.
 * ``image_sequence_attention.pt`` - image_parallel.SequenceAttention (the
   Flux/Qwen attention override: local queries, all-gathered keys/values)
   over image_layout.Layout for uneven image segments, W in {2,3,5}, with a
@@ -231,6 +235,53 @@ def main():
                     cases=scases), HERE / "sequence_attention.pt")
     torch.save(dict(q_lin=q_lin, k_lin=k_lin, v_lin=v_lin, wq=wq, wk=wk, freqs=freqs, eps=1e-6,
                     cases=tcases), HERE / "sequence_attention_token.pt")
+    # ------------------------------------------- self_attention_forward (B=2)
+    from powershard.operations import Linear
+    batch, n_total, heads, dim = 2, 300, 4, 128
+    hidden = heads * dim
+    g = torch.Generator().manual_seed(29)
+    x = torch.randn(batch, n_total, hidden, generator=g)
+    weights = [torch.randn(hidden, hidden, generator=g) * 0.02 for _ in range(4)]
+    biases = [torch.randn(hidden, generator=g) * 0.01 for _ in range(4)]
+    wq = torch.rand(hidden, generator=g) + 0.5
+    wk = torch.rand(hidden, generator=g) + 0.5
+    freqs = rope_table(n_total, dim // 2, 13)
+    fcases = []
+    for world in (1, 2):
+        cfg = DistributedConfig(attention_backend="math", sequence_mode="ulysses")
+
+        def rank_fn(rank):
+            a, b = shard_bounds(n_total, rank, world) if world > 1 else (0, n_total)
+            lin = []
+            for w, bias in zip(weights, biases):
+                layer = Linear(hidden, hidden, bias=True)
+                layer.weight.data.copy_(w)
+                layer.bias.data.copy_(bias)
+                lin.append(layer)
+            norm_q, norm_k = RMSNorm(hidden, eps=1e-6), RMSNorm(hidden, eps=1e-6)
+            norm_q.weight.data.copy_(wq)
+            norm_k.weight.data.copy_(wk)
+            state = wan_model.new_sequence_state(cfg)
+            state.update(total=n_total, enabled=world > 1, kv_collectives=0, kv_gathered_bytes=0,
+                         out_collectives=0, out_exchanged_bytes=0, padded_heads=0, scale_collectives=0)
+            mod = SimpleNamespace(num_heads=heads, head_dim=dim, norm_q=norm_q, norm_k=norm_k,
+                                  q=lin[0], k=lin[1], v=lin[2], o=lin[3], _ps_qk_scales=(1., 1., 1.),
+                                  _ps_sequence=state, _ps_attention=AttentionDispatcher(cfg),
+                                  _ps_group="wan_self", _ps_safe=False)
+            with torch.no_grad():
+                out = wan_model.self_attention_forward(mod, x[:, a:b], freqs[:, a:b])
+            counters = {key: state[key] for key in ("kv_collectives", "kv_gathered_bytes", "out_collectives",
+                                                    "out_exchanged_bytes", "padded_heads")}
+            return dict(bounds=(a, b), out=out, counters=counters)
+        if world == 1:
+            per_rank = [rank_fn(0)]
+        else:
+            with emulated_collectives(world) as run:
+                per_rank = run(rank_fn)
+        fcases.append(dict(world=world, ranks=per_rank))
+    torch.save(dict(x=x, weights=weights, biases=biases, wq=wq, wk=wk, freqs=freqs, heads=heads, eps=1e-6,
+                    cases=fcases), HERE / "self_attention_forward.pt")
+
     # ---------------------------------------- image Layout SequenceAttention
     from powershard import image_parallel
     from powershard.image_layout import Layout

@@ -38,6 +38,16 @@ def test_reference_arm_prints_one_contract_line():
     assert base["kind"] == "port" and base["value"] == line["value"] and base["cores"] >= 1 and base["sample"]
     assert line["e2e"]["value"] == line["value"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    # Every step's wall time is measured: the steps fit inside the arm's own run.
+    assert line["ms_per_step"] * line["steps"] / 1e3 <= line["run_s"]
+    # Same config object as the b200 arm of the same N, so the two lines compare.
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_module", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert line["config"] == json.loads(json.dumps(bench.workload_config(1)))
+    cfg0 = base["config0_gloo_w2"]
+    assert cfg0["world"] == 2 and cfg0["providers"]["math"]["ms_per_layer"] > 0
 
 
 def test_reference_arm_other_ranks_exit_quietly():

@@ -34,7 +34,7 @@ def test_exports_every_header_symbol(lib):
 
 def test_abi_version(lib):
     from powershard_b200 import _lib
-    assert lib.ps_b200_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.ps_b200_abi_version() == _lib.ABI_VERSION == 4
     assert lib.ps_b200_kernel_launches() == 0  # nothing launched without a GPU
 
 

@@ -33,7 +33,8 @@ def _setup_paths():
 
 
 class OracleKernels:
-    """Test stand-ins with the buffer contracts of powershard_b200.ops."""
+    """Test stand-ins with the buffer contracts of powershard_b200.ops
+    (unbatched and batched: a batched call is served row by row)."""
 
     class DeviceStatus:
         def __init__(self, device):
@@ -45,8 +46,13 @@ class OracleKernels:
         def check(self):
             pass
 
-    @staticmethod
-    def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+    @classmethod
+    def prepass(cls, x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+        if send.dim() == 6:
+            for b in range(send.shape[2]):
+                f = freqs[b] if freqs is not None and freqs.dim() == 5 else freqs
+                cls.prepass(x_q[b], x_k[b], x_v[b], w_q, w_k, f, send[:, :, b], geo, eps, norm_rope)
+            return
         from oracle import ulysses_oracle as oracle
         n, d = geo.n_local, geo.head_dim
         if norm_rope:
@@ -58,8 +64,14 @@ class OracleKernels:
         send.copy_(oracle.pack_qkv(q.to(send.dtype), k.to(send.dtype), v.to(send.dtype), geo.total, geo.rank,
                                    geo.world))
 
-    @staticmethod
-    def ulysses_attention(recv, out_send, geo, scale, status):
+    @classmethod
+    def ulysses_attention(cls, recv, out_send, geo, scale, status):
+        if recv.dim() == 6:
+            for b in range(recv.shape[2]):
+                row = out_send[:, b].clone()
+                cls.ulysses_attention(recv[:, :, b].contiguous(), row, geo, scale, status)
+                out_send[:, b] = row
+            return
         from oracle import ulysses_oracle as oracle
         q, k, v = oracle.unpack_qkv(recv, geo.total)
         o = oracle.sdpa_fp32(q[None], k[None], v[None], scale)[0]
@@ -67,8 +79,12 @@ class OracleKernels:
         hv = geo.heads_valid
         out_send[..., :hv, :] = packed[..., :hv, :]
 
-    @staticmethod
-    def unpack(out_recv, out, geo):
+    @classmethod
+    def unpack(cls, out_recv, out, geo):
+        if out_recv.dim() == 5:
+            for b in range(out_recv.shape[1]):
+                cls.unpack(out_recv[:, b].contiguous(), out[b], geo)
+            return
         from oracle import ulysses_oracle as oracle
         out.copy_(oracle.unpack_out(out_recv, geo.total, geo.heads, geo.rank, geo.world).to(out.dtype))
 
@@ -99,8 +115,14 @@ class LayoutKernels(OracleKernels):
     """Stand-ins driven by the geometry alone (any token split, including the
     image Layout's balanced one), for the pack-only and joint paths."""
 
-    @staticmethod
-    def prepass(x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+    @classmethod
+    def prepass(cls, x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True):
+        if send.dim() == 6:
+            for b in range(send.shape[2]):
+                row = send[:, :, b].clone()
+                cls.prepass(x_q[b], x_k[b], x_v[b], w_q, w_k, freqs, row, geo, eps, norm_rope)
+                send[:, :, b] = row
+            return
         assert not norm_rope, "layout stand-in packs pre-normalised inputs only"
         n, h, d = geo.n_local, geo.heads_per_rank, geo.head_dim
         send.zero_()
@@ -123,8 +145,12 @@ class LayoutKernels(OracleKernels):
             out_send[s, :valid[s], :hv] = o[row:row + valid[s]].to(out_send.dtype)
             row += valid[s]
 
-    @staticmethod
-    def unpack(out_recv, out, geo):
+    @classmethod
+    def unpack(cls, out_recv, out, geo):
+        if out_recv.dim() == 5:
+            for b in range(out_recv.shape[1]):
+                cls.unpack(out_recv[:, b], out[b], geo)
+            return
         h = geo.heads_per_rank
         for g in range(geo.heads):
             out[:, g] = out_recv[g // h, :geo.n_local, g % h].to(out.dtype)
@@ -356,6 +382,11 @@ class H3Kernels(OracleKernels):
 
     @classmethod
     def prepass(cls, x_q, x_k, x_v, w_q, w_k, freqs, send, geo, eps=1e-6, norm_rope=True, rope_split_pairs=None):
+        if send.dim() == 6:
+            for b in range(send.shape[2]):
+                cls.prepass(x_q[b], x_k[b], x_v[b], w_q, w_k, freqs, send[:, :, b], geo, eps, norm_rope,
+                            rope_split_pairs)
+            return
         from oracle import ulysses_oracle as oracle
         q, k, v = cls._normed(x_q, x_k, x_v, w_q, w_k, freqs, geo.heads, eps, norm_rope, rope_split_pairs)
         send.copy_(oracle.pack_qkv(q.to(send.dtype), k.to(send.dtype), v.to(send.dtype), geo.total, geo.rank,
@@ -468,4 +499,72 @@ def test_head_gather_over_gloo(world, total, batch, tmp_path, gloo_available):
     report = tmp_path / "report.json"
     mp.spawn(gather_worker, args=(world, str(tmp_path / "store"), str(report), total, batch), nprocs=world,
              join=True)
+    assert json.loads(report.read_text())["status"] == "PASS"
+
+
+def batch_worker(rank, world, store, report, golden):
+    """wan.self_attention_forward (the hook install_wan_compute sets,
+    powershard/wan_model.py:433-438) on a CFG batch of 2 rows over gloo,
+    against the reference's recording of the same layer: the whole batch
+    crosses in one exchange each way and the counters equal the reference's
+    (fp32 wire here, as recorded)."""
+    oracle = _setup_paths()
+    from powershard_b200 import wan
+    from powershard_b200.ulysses import UlyssesAttention
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=Path(store).as_uri(), rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        data = torch.load(golden, weights_only=False)
+        case = next(c for c in data["cases"] if c["world"] == world)
+        ref = case["ranks"][rank]
+        a, b = ref["bounds"]
+        heads, hidden = data["heads"], data["x"].shape[-1]
+        module = torch.nn.Module()
+        for name, w, bias in zip("qkvo", data["weights"], data["biases"]):
+            lin = torch.nn.Linear(hidden, hidden)
+            lin.weight.data.copy_(w)
+            lin.bias.data.copy_(bias)
+            setattr(module, name, lin)
+        module.norm_q = torch.nn.RMSNorm(hidden, eps=data["eps"])
+        module.norm_k = torch.nn.RMSNorm(hidden, eps=data["eps"])
+        module.norm_q.weight.data.copy_(data["wq"])
+        module.norm_k.weight.data.copy_(data["wk"])
+        module.num_heads, module.head_dim = heads, hidden // heads
+        state = dict(total=data["x"].shape[1], enabled=True, ulysses=True, comm_dtype="fp32", kv_collectives=0,
+                     kv_gathered_bytes=0, out_collectives=0, out_exchanged_bytes=0)
+        module._ps_sequence = state
+        engine = UlyssesAttention(kernels=OracleKernels)
+        calls = []
+        orig_exchange = engine._exchange
+
+        def counted_exchange(recv, send, geo):
+            calls.append(tuple(send.shape))
+            return orig_exchange(recv, send, geo)
+        engine._exchange = counted_exchange
+        module._ps_b200_engine = engine
+        wire = wan.WIRE_DTYPE
+        wan.WIRE_DTYPE = torch.float32  # the recording used the fp32 wire
+        try:
+            with torch.no_grad():
+                out = wan.self_attention_forward(module, data["x"][:, a:b], data["freqs"][:, a:b])
+        finally:
+            wan.WIRE_DTYPE = wire
+        err = (out - ref["out"]).abs()
+        assert float(err.max()) <= 2e-2 and float(err.mean() / ref["out"].abs().mean()) <= 5e-3
+        # one all_to_all each way, carrying both batch rows
+        assert len(calls) == 2 and calls[0][2] == 2 and calls[1][1] == 2, calls
+        for key in ("kv_collectives", "kv_gathered_bytes", "out_collectives", "out_exchanged_bytes",
+                    "padded_heads"):
+            assert state[key] == ref["counters"][key], (key, state[key], ref["counters"][key])
+        if rank == 0:
+            Path(report).write_text(json.dumps(dict(status="PASS")))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_self_attention_forward_cfg_batch_over_gloo(tmp_path, gloo_available):
+    report = tmp_path / "report.json"
+    golden = ROOT / "tests" / "golden" / "self_attention_forward.pt"
+    mp.spawn(batch_worker, args=(2, str(tmp_path / "store"), str(report), str(golden)), nprocs=2, join=True)
     assert json.loads(report.read_text())["status"] == "PASS"

@@ -198,3 +198,45 @@ def test_rope_split_half_matches_reference(oracle, golden_dir, index):
         assert float(diff.max()) <= float(case["out"].float().abs().max()) * 2 ** -7
     p = case["table"].shape[-3]
     assert torch.equal(got[..., 2 * p:], case["x"][..., 2 * p:])
+
+
+@pytest.mark.parametrize("index", range(2))
+def test_self_attention_forward_batch2_matches_reference(oracle, golden_dir, index):
+    """wan_model.self_attention_forward on a CFG batch of 2 (q/k/v/o Linear with
+    bias, attention_qkv, sequence_attention, o) restated with the oracle,
+    one batch row at a time, against the reference's recording (W = 1 with
+    the sequence state off, W = 2 Ulysses); the recorded counters count the
+    whole batch in one exchange, fp32 wire."""
+    import torch.nn.functional as F
+    data = load(golden_dir, "self_attention_forward.pt")
+    case = data["cases"][index]
+    world, heads = case["world"], data["heads"]
+    x = data["x"]
+    batch, total, hidden = x.shape
+    # Projections per rank shard, as each rank of the reference computes them
+    # (the BLAS blocking of a shard differs from that of the whole sequence).
+    bounds = [oracle.shard_bounds(total, r, world) for r in range(world)]
+    lin = [torch.cat([F.linear(x[:, a:z], w, b) for a, z in bounds], dim=1)
+           for w, b in zip(data["weights"][:3], data["biases"][:3])]
+    # The reference's power-of-two V scale covers the whole batch a rank receives.
+    h = -(-heads // world)
+    v_all = lin[2].view(batch, total, heads, -1)
+    v_scales = [oracle._power2_scale(v_all[:, :, r * h:(r + 1) * h].abs().amax() / 16384.0)
+                for r in range(world)]
+    rows = []
+    for b in range(batch):
+        outs = oracle.sequence_attention(lin[0][b:b + 1], lin[1][b:b + 1], lin[2][b:b + 1], data["wq"], data["wk"],
+                                         data["freqs"], heads, world, data["eps"], wire_dtype=torch.float32,
+                                         attention="math", provider_dtype=torch.float16, v_scales=v_scales)
+        rows.append(outs)
+    for r, ref in enumerate(case["ranks"]):
+        a, bnd = ref["bounds"]
+        attn = torch.cat([rows[b][r] for b in range(batch)]).reshape(batch, bnd - a, hidden)
+        out = F.linear(attn, data["weights"][3], data["biases"][3])
+        torch.testing.assert_close(out, ref["out"], atol=2e-6, rtol=1e-5)
+        if world > 1:
+            width, h = -(-total // world), -(-heads // world)
+            c = ref["counters"]
+            assert c["kv_collectives"] == 1 and c["out_collectives"] == 1
+            assert c["kv_gathered_bytes"] == world * 3 * batch * width * h * 128 * 4
+            assert c["out_exchanged_bytes"] == world * batch * width * h * 128 * 4
