@@ -299,13 +299,13 @@ def check_parity(engine_out, proj, norm_w, geo, grid, world, rank, dev, nccl_out
 def received_qkv(engine, geo, dev):
     """This rank's post-exchange q/k/v [1, h_valid, L, D] (contiguous copies of
     the receive buffer the attention kernel reads)."""
-    px = engine._peer(geo, torch.bfloat16, dev)
-    recv = px.recv if px is not None else engine._workspace(geo, torch.bfloat16, dev)[0]["recv"]
-    w, _, width, h, d = recv.shape
+    px = engine._peer(geo, torch.bfloat16, dev, batch=1)
+    recv = px.recv if px is not None else engine._workspace(geo, torch.bfloat16, dev, 1)[0]["recv"]
+    w, _, _, width, h, d = recv.shape  # [W, 3, B=1, width, h, D]
     hv = geo.heads_valid
     out = []
     for i in range(3):
-        t = recv[:, i].reshape(w * width, h, d)[:geo.total, :hv]
+        t = recv[:, i, 0].reshape(w * width, h, d)[:geo.total, :hv]
         out.append(t.permute(1, 0, 2).unsqueeze(0).contiguous())
     return out
 
@@ -357,21 +357,23 @@ def measure_comm(engine, proj, norm_w, freqs, geo, dev, ms_step, attn_ms):
         torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[dev.index])
 
-    px = engine._peer(geo, torch.bfloat16, dev)
+    px = engine._peer(geo, torch.bfloat16, dev, batch=1)  # the buffers the timed steps used
     if px is not None:
         local_blocks = [local_stage.data_ptr() + r * geo.heads_per_rank * DIM * esize for r in range(world)]
+        xb = [t[None] for t in proj]
         sync_all()
-        t_pre_to = time_events(lambda: ops.prepass_to(*proj, norm_w, norm_w, freqs, px.dst_blocks, geo,
-                                                      torch.bfloat16), reps=5)
+        t_pre_to = time_events(lambda: ops.prepass_to(*xb, norm_w, norm_w, freqs, px.dst_blocks, geo,
+                                                      torch.bfloat16, batch=1), reps=5)
         sync_all()
         t_pre_loc = time_events(lambda: ops.prepass(*proj, norm_w, norm_w, freqs, local_send, geo), reps=5)
         sync_all()
+        attn = dict(workspace=ws, batch=1, out_batch_stride=px.out_batch_stride)
         t_att_to = time_events(lambda: ops.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride,
-                                                                torch.bfloat16, geo, scale, status, workspace=ws),
+                                                                torch.bfloat16, geo, scale, status, **attn),
                                reps=3, warm=1)
         sync_all()
         t_att_loc = time_events(lambda: ops.ulysses_attention_to(px.recv, local_blocks, px.out_row_stride,
-                                                                 torch.bfloat16, geo, scale, status, workspace=ws),
+                                                                 torch.bfloat16, geo, scale, status, **attn),
                                 reps=3, warm=1)
         sync_all()
         res["peer"] = dict(prepass_to_ms=t_pre_to, prepass_local_ms=t_pre_loc, attn_to_ms=t_att_to,

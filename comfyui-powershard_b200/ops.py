@@ -226,8 +226,8 @@ def ulysses_attention(recv, out_send, geo: UlyssesGeometry, scale: float, status
         if tuple(out_send.shape) != geo.out_shape(batch) or not out_send.is_contiguous():
             raise ValueError(f"attention: out must be contiguous {geo.out_shape(batch)}")
         h, d = geo.heads_per_rank, geo.head_dim
-        ulysses_attention_to(recv, send_blocks(out_send), h * d, out_send.dtype, geo, scale, status, workspace,
-                             batch=batch, out_batch_stride=geo.width * h * d)
+        _attention_batch(recv, send_blocks(out_send), geo.width * h * d, h * d, out_send.dtype, geo, batch, scale,
+                         status, workspace)
         return
     if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
         raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")
@@ -300,6 +300,28 @@ def unpack(out_recv, out, geo: UlyssesGeometry):
     _lib.check(rc, "ps_b200_unpack")
 
 
+def _attention_batch(recv, out_blocks, out_batch_stride: int, out_row_stride: int, out_dtype: torch.dtype,
+                     geo: UlyssesGeometry, batch: int, scale: float, status: DeviceStatus | None, workspace=None):
+    """Attention over the batched receive buffer [W, 3, B, width, h, D]; batch
+    row b, valid row i of segment s, head j -> out_blocks[s] + b*out_batch_stride
+    + i*out_row_stride + j*D elements (ps_b200_ulysses_attn_batch)."""
+    lib = _lib.load()
+    if tuple(recv.shape) != geo.send_shape(batch) or not recv.is_contiguous():
+        raise ValueError(f"attention: recv must be contiguous {geo.send_shape(batch)}")
+    if len(out_blocks) != geo.world:
+        raise ValueError(f"attention: {len(out_blocks)} output blocks for {geo.world} ranks")
+    if out_dtype not in (recv.dtype, torch.float32):
+        raise ValueError("attention: output dtype must be fp32 or the input dtype")
+    rc = lib.ps_b200_ulysses_attn_batch(
+        recv.data_ptr(), _lib.ptrs(out_blocks), int(out_batch_stride), int(out_row_stride),
+        _lib.dtype_code(recv.dtype), _lib.dtype_code(out_dtype), int(batch), geo.world, geo.width, geo.total,
+        _seg_table(geo), geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale), *_ws(workspace),
+        status.ptr if status is not None else None, _lib.stream_handle(recv.device))
+    _lib.check(rc, "ps_b200_ulysses_attn_batch")
+    if status is not None:
+        status.arm()
+
+
 def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch.dtype, geo: UlyssesGeometry,
                          scale: float, status: DeviceStatus | None, workspace=None, batch: int | None = None,
                          out_batch_stride: int = 0):
@@ -311,20 +333,8 @@ def ulysses_attention_to(recv, out_blocks, out_row_stride: int, out_dtype: torch
     lib = _lib.load()
     _check16(recv, "attention recv")
     if batch is not None:
-        if tuple(recv.shape) != geo.send_shape(batch) or not recv.is_contiguous():
-            raise ValueError(f"attention: recv must be contiguous {geo.send_shape(batch)}")
-        if len(out_blocks) != geo.world:
-            raise ValueError(f"attention: {len(out_blocks)} output blocks for {geo.world} ranks")
-        if out_dtype not in (recv.dtype, torch.float32):
-            raise ValueError("attention: output dtype must be fp32 or the input dtype")
-        rc = lib.ps_b200_ulysses_attn_batch(
-            recv.data_ptr(), _lib.ptrs(out_blocks), int(out_batch_stride), int(out_row_stride),
-            _lib.dtype_code(recv.dtype), _lib.dtype_code(out_dtype), int(batch), geo.world, geo.width, geo.total,
-            _seg_table(geo), geo.heads_per_rank, geo.heads_valid, geo.head_dim, float(scale), *_ws(workspace),
-            status.ptr if status is not None else None, _lib.stream_handle(recv.device))
-        _lib.check(rc, "ps_b200_ulysses_attn_batch")
-        if status is not None:
-            status.arm()
+        _attention_batch(recv, out_blocks, out_batch_stride, out_row_stride, out_dtype, geo, int(batch), scale,
+                         status, workspace)
         return
     if tuple(recv.shape) != geo.send_shape() or not recv.is_contiguous():
         raise ValueError(f"attention: recv must be contiguous {geo.send_shape()}")

@@ -134,3 +134,57 @@ def test_image_override_over_nccl(world, prefix, image, heads, tmp_path, cuda_li
     for rank in range(world):
         data = json.loads(Path(f"{report}.{rank}").read_text())
         assert data["ok"], data
+
+
+def batch_worker(rank, world, port, report, total, heads, exchange):
+    """A CFG batch of 2 rows through forward_batch: one exchange each way for
+    the batch (both exchanges), against the oracle row by row."""
+    import sys
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import ulysses_oracle as oracle
+    from powershard_b200.ulysses import UlyssesAttention
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        g = torch.Generator().manual_seed(8)
+        x = [(torch.randn(2, total, heads * 128, generator=g) * 1.4).to(torch.bfloat16) for _ in range(3)]
+        w = torch.rand(heads * 128, generator=g) + 0.5
+        freqs = oracle.rope_table_3d((total // 100 + 1, 10, 10), 128)[:, :total]
+        a, b = oracle.shard_bounds(total, rank, world)
+        engine = UlyssesAttention(exchange=exchange)
+        state = {}
+        out = engine.forward_batch(*(t[:, a:b].to(dev) for t in x), w.to(dev), w.to(dev), freqs[0, a:b, 0].to(dev),
+                                   total=total, heads=heads, state=state)
+        engine.check()
+        errs = []
+        for row in range(2):
+            expected = oracle.sequence_attention(x[0][row:row + 1], x[1][row:row + 1], x[2][row:row + 1], w, w,
+                                                 freqs, heads, world)[rank][0].float()
+            err = (out[row].float().cpu() - expected).abs()
+            errs.append((float(err.max()), float(err.mean() / expected.abs().mean())))
+        ok = all(e <= 2e-2 and r <= 5e-3 for e, r in errs)
+        ok = ok and state["kv_collectives"] == 1 and state["exchange"] == exchange
+        ok = ok and state["kv_gathered_bytes"] == world * 3 * 2 * (-(-total // world)) * (-(-heads // world)) * 128 * 2
+        engine.close()
+        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, errs=errs, rank=rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("world,total,heads", [(2, 1000, 40), (4, 1023, 24)])
+def test_cfg_batch_over_nccl(world, total, heads, exchange, tmp_path, cuda_lib):
+    """Both exchanges with a batch of 2 rows in one call (the reference's
+    batched packing, powershard/wan_model.py:356-362)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"NOT_RUN: needs {world} GPUs, box has {torch.cuda.device_count()}")
+    report = tmp_path / "r"
+    mp.spawn(batch_worker, args=(world, _free_port(), str(report), total, heads, exchange), nprocs=world, join=True)
+    for rank in range(world):
+        data = json.loads(Path(f"{report}.{rank}").read_text())
+        assert data["ok"], data
