@@ -361,23 +361,23 @@ def measure_comm(engine, proj, norm_w, freqs, geo, dev, ms_step, attn_ms):
     if px is not None:
         local_blocks = [local_stage.data_ptr() + r * geo.heads_per_rank * DIM * esize for r in range(world)]
         xb = [t[None] for t in proj]
-        sync_all()
-        t_pre_to = time_events(lambda: ops.prepass_to(*xb, norm_w, norm_w, freqs, px.dst_blocks, geo,
-                                                      torch.bfloat16, batch=1), reps=5)
-        sync_all()
-        t_pre_loc = time_events(lambda: ops.prepass(*proj, norm_w, norm_w, freqs, local_send, geo), reps=5)
-        sync_all()
         attn = dict(workspace=ws, batch=1, out_batch_stride=px.out_batch_stride)
-        t_att_to = time_events(lambda: ops.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride,
-                                                                torch.bfloat16, geo, scale, status, **attn),
-                               reps=3, warm=1)
+        runs = dict(
+            prepass_to=lambda: ops.prepass_to(*xb, norm_w, norm_w, freqs, px.dst_blocks, geo, torch.bfloat16, batch=1),
+            prepass_local=lambda: ops.prepass(*proj, norm_w, norm_w, freqs, local_send, geo),
+            attn_to=lambda: ops.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, torch.bfloat16, geo,
+                                                     scale, status, **attn),
+            attn_local=lambda: ops.ulysses_attention_to(px.recv, local_blocks, px.out_row_stride, torch.bfloat16,
+                                                        geo, scale, status, **attn))
+        # Peer-storing and local-storing launches alternate (same clocks and
+        # power state for both); each figure is the median of its launches.
+        samples = {k: [] for k in runs}
+        for rep in range(4):
+            for name in ("prepass_to", "prepass_local", "attn_to", "attn_local"):
+                sync_all()
+                samples[name].append(time_events(runs[name], reps=1, warm=1 if rep == 0 else 0))
         sync_all()
-        t_att_loc = time_events(lambda: ops.ulysses_attention_to(px.recv, local_blocks, px.out_row_stride,
-                                                                 torch.bfloat16, geo, scale, status, **attn),
-                                reps=3, warm=1)
-        sync_all()
-        res["peer"] = dict(prepass_to_ms=t_pre_to, prepass_local_ms=t_pre_loc, attn_to_ms=t_att_to,
-                           attn_local_ms=t_att_loc)
+        res["peer"] = {f"{k}_ms": statistics.median(v) for k, v in samples.items()}
     recv = torch.empty_like(local_send)
     out_send = torch.empty(geo.out_shape(), dtype=torch.bfloat16, device=dev)
     out_recv = torch.empty_like(out_send)

@@ -24,6 +24,12 @@ inputs + outputs with torch.save next to this script:
   operations.Linear + RMSNorm, attention_qkv, sequence_attention, o) on a
   CFG batch of 2 rows, W=1 (sequence state off, math provider) and Ulysses
   W=2 (math provider, fp32 wire), with the state counters of each rank.
+* ``wan_backend_call.pt`` - wan_backend.WanBackend.call (the worker's forward
+  command) over a two-block stand-in network whose blocks run the
+  reference's self_attention_forward with residuals and whose forward keeps
+  the sequence state as wan_forward does (counters reset, head gather), at
+  W=2 in Ulysses and token mode (math provider, fp32 wire): the output of
+  each rank, the state after the forward and metrics["sequence_communication"].
 * ``image_sequence_attention.pt`` - image_parallel.SequenceAttention (the
   Flux/Qwen attention override: local queries, all-gathered keys/values)
   over image_layout.Layout for uneven image segments, W in {2,3,5}, with a
@@ -281,6 +287,95 @@ def main():
         fcases.append(dict(world=world, ranks=per_rank))
     torch.save(dict(x=x, weights=weights, biases=biases, wq=wq, wk=wk, freqs=freqs, heads=heads, eps=1e-6,
                     cases=fcases), HERE / "self_attention_forward.pt")
+
+    # ------------------------------------------------------ WanBackend.call
+    from powershard import wan_backend
+    bcases = []
+    n_tok, n_blocks, heads = 96, 2, 2
+    hidden = heads * dim
+    g = torch.Generator().manual_seed(37)
+    xw = torch.randn(1, n_tok, hidden, generator=g)
+    bweights = [[torch.randn(hidden, hidden, generator=g) * 0.02 for _ in range(4)] for _ in range(n_blocks)]
+    bnorm = [(torch.rand(hidden, generator=g) + 0.5, torch.rand(hidden, generator=g) + 0.5) for _ in range(n_blocks)]
+    bfreqs = rope_table(n_tok, dim // 2, 17)
+    saved_sharded = wan_backend.assert_sharded
+    wan_backend.assert_sharded = lambda root, cpu_offload=None: None  # the stand-in root holds no FSDP shards
+    try:
+        for mode in ("ulysses", "token"):
+            world = 2
+            cfg = DistributedConfig(attention_backend="math", sequence_mode=mode)
+
+            def rank_fn(rank):
+                state = wan_model.new_sequence_state(cfg)
+                blocks = []
+                for ws, (wq_, wk_) in zip(bweights, bnorm):
+                    lin = []
+                    for w in ws:
+                        layer = Linear(hidden, hidden, bias=True)
+                        layer.weight.data.copy_(w)
+                        layer.bias.data.zero_()
+                        lin.append(layer)
+                    norm_q, norm_k = RMSNorm(hidden, eps=1e-6), RMSNorm(hidden, eps=1e-6)
+                    norm_q.weight.data.copy_(wq_)
+                    norm_k.weight.data.copy_(wk_)
+                    blocks.append(SimpleNamespace(num_heads=heads, head_dim=dim, norm_q=norm_q, norm_k=norm_k,
+                                                  q=lin[0], k=lin[1], v=lin[2], o=lin[3], _ps_qk_scales=(1., 1., 1.),
+                                                  _ps_sequence=state, _ps_attention=AttentionDispatcher(cfg),
+                                                  _ps_group="wan_self", _ps_safe=False))
+
+                def forward(x):
+                    # The sequence handling of wan_forward (wan_model.py:1004-1011, :1073-1075).
+                    total = x.shape[1]
+                    state.update(total=total, enabled=world > 1, kv_collectives=0, kv_gathered_bytes=0,
+                                 out_collectives=0, out_exchanged_bytes=0, scale_collectives=0, head_gathers=0)
+                    a, b = shard_bounds(total, rank, world)
+                    local = x[:, a:b]
+                    for blk in blocks:
+                        local = local + wan_model.self_attention_forward(blk, local, bfreqs[:, a:b])
+                    out = wan_model.gather_tokens(local, total)
+                    state["head_gathers"] += 1
+                    return out
+
+                class Root:
+                    network = SimpleNamespace(blocks=blocks, num_heads=heads)
+
+                    def __call__(self, command, args, kwargs):
+                        return forward(*args)
+
+                    def modules(self):
+                        return iter(())
+
+                    def named_modules(self):
+                        return iter(())
+
+                    def named_parameters(self):
+                        return iter(())
+
+                stub = lambda **kw: SimpleNamespace(**kw)  # noqa: E731
+                backend = stub(
+                    device=torch.device("cpu"), slot="main", world=world, sequence=state, root=Root(), units=[],
+                    config=stub(reserve_gib=0.0, backend="fsdp2_sequence", cpu_offload=False, weight_placement="gpu"),
+                    plan_memory=lambda args: dict(effective_prefetch=0),
+                    ledger=stub(reset=lambda: None, report=lambda: {}),
+                    tracker=stub(begin=lambda device: None, finish=lambda result: None),
+                    attention=stub(report=lambda: {}), identity={}, lora_report=[],
+                    spectrum=stub(report=lambda: {}), managed_pool=None, shard_bytes=0, buffer_bytes=0,
+                    group_bytes=[0], options=stub(fp16_safe=False))
+                with torch.no_grad():
+                    out, metrics = wan_backend.WanBackend.call(backend, "forward", (xw,), {})
+                keep = ("total", "enabled", "ulysses", "kv_collectives", "kv_gathered_bytes", "out_collectives",
+                        "out_exchanged_bytes", "scale_collectives", "head_gathers", "padded_heads",
+                        "effective_comm_dtype")
+                return dict(out=out, state={k: state[k] for k in keep if k in state},
+                            sequence_communication=metrics["sequence_communication"],
+                            local_token_range=metrics["local_token_range"])
+            with emulated_collectives(world) as run:
+                per_rank = run(rank_fn)
+            bcases.append(dict(mode=mode, world=world, ranks=per_rank))
+    finally:
+        wan_backend.assert_sharded = saved_sharded
+    torch.save(dict(x=xw, weights=bweights, norms=bnorm, freqs=bfreqs, heads=heads, eps=1e-6, cases=bcases),
+               HERE / "wan_backend_call.pt")
 
     # ---------------------------------------- image Layout SequenceAttention
     from powershard import image_parallel
