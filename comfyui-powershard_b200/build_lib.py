@@ -15,7 +15,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
-SOURCES = ["csrc/attention.cu", "csrc/prepass.cu", "csrc/capi.cu", "csrc/static_block.cu", "csrc/selftest.cu"]
+SOURCES = ["csrc/attention.cu", "csrc/prepass.cu", "csrc/proj.cu", "csrc/capi.cu", "csrc/static_block.cu",
+           "csrc/selftest.cu"]
 HEADERS = ["csrc/ptx.cuh", "csrc/internal.h"]
 OUTPUT = HERE / "lib" / "libps_b200.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

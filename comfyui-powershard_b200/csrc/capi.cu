@@ -709,3 +709,204 @@ int ps_b200_ipc_close(void* ptr) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ projection GEMMs
+namespace psb {
+namespace {
+
+// 2-D map over [rows][cols] 16-bit elements (row stride in elements), box
+// 64 columns x box_rows rows, 128-byte swizzle.
+int make_map_2d(CUtensorMap* m, const void* base, bool fp16, int64_t cols, int64_t rows, int64_t row_stride,
+                unsigned box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(PS_B200_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (row_stride * 2 % 16 != 0 || row_stride <= 0)
+    return set_error(PS_B200_ERR_INVALID, "row stride of %lld elements is not a positive multiple of 8",
+                     (long long)row_stride);
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(row_stride * 2)};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PS_B200_ERR_INVALID, "cuTensorMapEncodeTiled (2-D) failed with CUresult %d", int(r));
+  return PS_B200_OK;
+}
+
+// 3-D map over [blocks][rows][cols] (strides in elements), box 64 x 128 x 1.
+int make_map_3d(CUtensorMap* m, const void* base, bool fp16, int64_t cols, int64_t rows, int64_t blocks,
+                int64_t row_stride, int64_t block_stride) {
+  auto fn = encode_fn();
+  if (!fn) return set_error(PS_B200_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if (row_stride <= 0 || row_stride % 8 != 0 || block_stride <= 0 || block_stride % 8 != 0)
+    return set_error(PS_B200_ERR_INVALID, "exchange-buffer strides must be positive multiples of 8 elements");
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(rows), cuuint64_t(blocks)};
+  cuuint64_t strides[2] = {cuuint64_t(row_stride * 2), cuuint64_t(block_stride * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(PS_B200_ERR_INVALID, "cuTensorMapEncodeTiled (3-D) failed with CUresult %d", int(r));
+  return PS_B200_OK;
+}
+
+int proj_ctas() { return sm_count(); }
+
+int64_t qkv_rows_blocks(int n) { return (int64_t(n) + 127) / 128; }
+
+}  // namespace
+}  // namespace psb
+
+extern "C" {
+
+size_t ps_b200_qkv_proj_workspace_bytes(int n_local, int heads, int head_dim) {
+  if (n_local <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  const int64_t width = int64_t(heads) * head_dim;
+  const int64_t groups = 2 * psb::qkv_rows_blocks(n_local);
+  const int64_t part = groups * (width / 256) * 128 * 4;
+  return static_cast<size_t>(((part + 255) / 256) * 256 + ((groups * 4 + 255) / 256) * 256);
+}
+
+int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const void* w_k, const void* w_v,
+                     const void* b_q, const void* b_k, const void* b_v, int b_dtype, const void* w_qnorm,
+                     const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_row_stride,
+                     void* const* dst_blocks, int dtype, int world, int n_local, int seg_rows, int heads,
+                     int heads_per_rank, int head_dim, int in_features, float eps, void* workspace,
+                     size_t workspace_bytes, int* status, void* stream) {
+  using namespace psb;
+  if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "projection supports bf16 and fp16 only");
+  if (world < 1 || world > kMaxSegs || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
+      int64_t(heads_per_rank) * world < heads || in_features <= 0)
+    return set_error(PS_B200_ERR_INVALID, "inconsistent projection geometry");
+  if (head_dim != 128) return set_error(PS_B200_ERR_UNSUPPORTED, "projection supports head_dim 128 only");
+  const int64_t width = int64_t(heads) * head_dim;
+  if (width % 256 != 0) return set_error(PS_B200_ERR_UNSUPPORTED, "projection needs an even head count");
+  if (in_features % 64 != 0) return set_error(PS_B200_ERR_UNSUPPORTED, "in_features must be a multiple of 64");
+  if (b_dtype != dtype && b_dtype != PS_B200_FP32) return set_error(PS_B200_ERR_UNSUPPORTED, "bias dtype");
+  if (w_dtype != dtype && w_dtype != PS_B200_FP32) return set_error(PS_B200_ERR_UNSUPPORTED, "norm weight dtype");
+  if (!std::isfinite(eps) || eps < 0.f) return set_error(PS_B200_ERR_INVALID, "eps must be finite and >= 0");
+  if (seg_rows == 0) return PS_B200_OK;
+  if (!dst_blocks) return set_error(PS_B200_ERR_INVALID, "null destination table");
+  for (int d = 0; d < world; ++d)
+    if (!dst_blocks[d] || !aligned16(dst_blocks[d]))
+      return set_error(PS_B200_ERR_INVALID, "destination block %d null or not 16-byte aligned", d);
+  ProjArgs a{};
+  a.n = n_local;
+  a.kdim = in_features;
+  a.width = static_cast<int>(width);
+  a.ntile_n = static_cast<int>(width / 256);
+  a.row_blocks = static_cast<int>(qkv_rows_blocks(n_local));
+  a.epi = 1;
+  a.bias[0] = b_q;
+  a.bias[1] = b_k;
+  a.bias[2] = b_v;
+  a.bias_fp32 = b_dtype == PS_B200_FP32;
+  a.normw[0] = w_qnorm;
+  a.normw[1] = w_knorm;
+  a.normw_fp32 = w_dtype == PS_B200_FP32;
+  a.freqs = freqs;
+  a.freqs_row_stride = freqs_row_stride;
+  a.eps = eps;
+  for (int d = 0; d < world; ++d) a.dst[d] = dst_blocks[d];
+  a.world = world;
+  a.seg_rows = seg_rows;
+  a.heads = heads;
+  a.heads_per_rank = heads_per_rank;
+  a.head_dim = head_dim;
+  a.status = status;
+  if (n_local > 0) {
+    if (!x || !w_q || !w_k || !w_v || !w_qnorm || !w_knorm || !freqs || !aligned16(x) || !aligned16(w_q) ||
+        !aligned16(w_k) || !aligned16(w_v) || !aligned16(w_qnorm) || !aligned16(w_knorm) || !aligned16(freqs) ||
+        freqs_row_stride % 4 != 0 || freqs_row_stride < head_dim * 2)
+      return set_error(PS_B200_ERR_INVALID, "projection inputs must be non-null and 16-byte aligned");
+    for (const void* b : {b_q, b_k, b_v})
+      if (b && !aligned16(b)) return set_error(PS_B200_ERR_INVALID, "bias must be 16-byte aligned");
+    const size_t need = ps_b200_qkv_proj_workspace_bytes(n_local, heads, head_dim);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return set_error(PS_B200_ERR_INVALID, "projection workspace of %zu bytes required", need);
+    if (int rc = check_device()) return rc;
+    const int ctas = proj_ctas();
+    const int G = a.ntile_n;
+    if (G > ctas) return set_error(PS_B200_ERR_UNSUPPORTED, "projection width above %d columns", ctas * 256);
+    a.total_groups = 2 * a.row_blocks;
+    a.groups_per_round = ctas / G;
+    a.total_tiles = a.row_blocks * G;  // v tiles
+    const int rg = (a.total_groups + a.groups_per_round - 1) / a.groups_per_round;
+    const int64_t v_in_group_rounds = int64_t(rg) * ctas - int64_t(a.total_groups) * G;
+    const int64_t v_left = a.total_tiles - v_in_group_rounds;
+    a.rounds = rg + static_cast<int>(v_left > 0 ? (v_left + ctas - 1) / ctas : 0);
+    a.ss_part = static_cast<float*>(workspace);
+    const int64_t part_bytes = ((int64_t(a.total_groups) * G * 128 * 4 + 255) / 256) * 256;
+    a.counters = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + part_bytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaMemsetAsync(a.counters, 0, size_t(a.total_groups) * 4, s);
+    if (err != cudaSuccess) return set_cuda_error("projection: clearing the group counters", err);
+    const bool fp16 = dtype == PS_B200_FP16;
+    CUtensorMap ta, tw[3];
+    if (int rc = make_map_2d(&ta, x, fp16, in_features, n_local, x_row_stride, 128)) return rc;
+    const void* ws[3] = {w_q, w_k, w_v};
+    for (int i = 0; i < 3; ++i)
+      if (int rc = make_map_2d(&tw[i], ws[i], fp16, in_features, width, in_features, 256)) return rc;
+    return launch_proj(ta, tw[0], tw[1], tw[2], a, fp16, ctas, s);
+  }
+  // No local rows: only the zero padding of the send blocks.
+  if (int rc = check_device()) return rc;
+  CUtensorMap none{};
+  return launch_proj(none, none, none, none, a, dtype == PS_B200_FP16, 1, static_cast<cudaStream_t>(stream));
+}
+
+int ps_b200_out_proj(const void* src, int64_t src_row_stride, int64_t src_block_stride, int src_block_cols,
+                     const void* w_o, const void* b_o, int b_dtype, void* out, int64_t out_row_stride, int dtype,
+                     int out_dtype, int n_local, int in_features, int out_features, int* status, void* stream) {
+  using namespace psb;
+  if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "projection supports bf16 and fp16 only");
+  if (out_dtype != dtype && out_dtype != PS_B200_FP32)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "projection output must be fp32 or the input dtype");
+  if (n_local < 0 || in_features <= 0 || out_features <= 0) return set_error(PS_B200_ERR_INVALID, "negative size");
+  if (in_features % 64 != 0 || out_features % 256 != 0)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "projection needs in_features %% 64 == 0 and out_features %% 256 == 0");
+  if (b_dtype != dtype && b_dtype != PS_B200_FP32) return set_error(PS_B200_ERR_UNSUPPORTED, "bias dtype");
+  if (n_local == 0) return PS_B200_OK;
+  if (!src || !w_o || !out || !aligned16(src) || !aligned16(w_o) || !aligned16(out) || (b_o && !aligned16(b_o)) ||
+      out_row_stride % 8 != 0 || out_row_stride < out_features)
+    return set_error(PS_B200_ERR_INVALID, "projection buffers must be 16-byte aligned, strides %% 8 == 0");
+  const bool blocks = src_block_cols > 0;
+  // Blocks may end short of src_block_cols in the last one (padded heads of the
+  // NCCL receive layout): the K loop stops at in_features.
+  if (blocks && src_block_cols % 64 != 0)
+    return set_error(PS_B200_ERR_UNSUPPORTED, "source blocks must hold a multiple of 64 columns");
+  if (int rc = check_device()) return rc;
+  ProjArgs a{};
+  a.n = n_local;
+  a.kdim = in_features;
+  a.width = out_features;
+  a.ntile_n = out_features / 256;
+  a.row_blocks = static_cast<int>(qkv_rows_blocks(n_local));
+  a.a_mode = blocks ? 1 : 0;
+  a.a_block_k = blocks ? src_block_cols : 0;
+  a.epi = 0;
+  a.bias[0] = b_o;
+  a.bias_fp32 = b_dtype == PS_B200_FP32;
+  a.out = out;
+  a.out_row_stride = out_row_stride;
+  a.out_fp32 = out_dtype == PS_B200_FP32;
+  a.status = status;
+  a.total_tiles = a.row_blocks * a.ntile_n;
+  const int ctas = proj_ctas();
+  a.rounds = (a.total_tiles + ctas - 1) / ctas;
+  const bool fp16 = dtype == PS_B200_FP16;
+  CUtensorMap ta, tw;
+  if (blocks) {
+    const int64_t nblocks = (in_features + src_block_cols - 1) / src_block_cols;
+    if (int rc = make_map_3d(&ta, src, fp16, src_block_cols, n_local, nblocks, src_row_stride, src_block_stride))
+      return rc;
+  } else {
+    if (int rc = make_map_2d(&ta, src, fp16, in_features, n_local, src_row_stride, 128)) return rc;
+  }
+  if (int rc = make_map_2d(&tw, w_o, fp16, in_features, out_features, in_features, 256)) return rc;
+  return launch_proj(ta, tw, tw, tw, a, fp16, ctas, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

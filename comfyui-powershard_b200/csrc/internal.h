@@ -98,6 +98,42 @@ struct UnpackArgs {
 
 int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream);
 
+// Arguments of the projection GEMMs (proj.cu) that are not tensor maps.
+struct ProjArgs {
+  int n;                   // rows of A (this rank's tokens)
+  int kdim;                // K: input features (a multiple of 64)
+  int width;               // output features of one projection (a multiple of 256)
+  int ntile_n;             // width / 256: column tiles of one projection
+  int row_blocks;          // ceil(n / 128)
+  int a_mode;              // 0: A is [n][kdim] rows; 1: A is [src][n][a_block_k] blocks (k = src*a_block_k + c)
+  int a_block_k;           // columns per source block (a multiple of 64) for a_mode 1
+  int epi;                 // 0: y = A W^T + b stored row-major; 1: q/k/v with RMSNorm, RoPE and the Ulysses pack
+  const void* bias[3];     // per projection, [width], may be null
+  int bias_fp32;           // 1: fp32 biases, 0: the 16-bit activation type
+  const void* normw[2];    // RMSNorm weights of q and k, [width]
+  int normw_fp32;
+  const float* freqs;      // [n][head_dim/2][2][2] rotation table
+  int64_t freqs_row_stride;
+  float eps;
+  void* dst[kMaxSegs];     // epi 1: destination d's block [3][seg_rows][heads_per_rank][head_dim]
+  int world, seg_rows, heads, heads_per_rank, head_dim;
+  void* out;               // epi 0: [n][width] (row stride out_row_stride elements)
+  int64_t out_row_stride;
+  int out_fp32;
+  // Scheduling (persistent CTAs, one task = one 128 x 256 tile per round):
+  int groups_per_round;    // epi 1: whole q/k groups (ntile_n tiles of one row block) per round
+  int total_groups;        // epi 1: 2 * row_blocks
+  int total_tiles;         // epi 0: row_blocks * ntile_n; epi 1: v tiles, row_blocks * ntile_n
+  int rounds;
+  float* ss_part;          // epi 1: [total_groups][ntile_n][128] partial sums of squares
+  unsigned* counters;      // epi 1: [total_groups] tiles of the group that posted their partials (zeroed)
+  int* status;             // device status word, may be null
+};
+
+// Launches the projection GEMM (cooperative: every CTA resident, one per SM).
+int launch_proj(const CUtensorMap& ta, const CUtensorMap& tw0, const CUtensorMap& tw1, const CUtensorMap& tw2,
+                const ProjArgs& args, bool fp16, int ctas, cudaStream_t stream);
+
 struct BroadcastArgs {
   const void* src;         // 16-byte vectors to copy
   void* dst[kMaxSegs];     // destinations (this GPU's memory or a peer's)

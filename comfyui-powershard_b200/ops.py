@@ -532,3 +532,95 @@ def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None, work
     _lib.check(rc, "ps_b200_attn_fwd")
     if status is not None:
         status.arm()
+
+
+# ------------------------------------------------------------ projection GEMMs
+def projection_workspace(n_local: int, heads: int, head_dim: int, device: torch.device) -> torch.Tensor:
+    """Scratch of ``qkv_projection`` (per-row partial sums of squares and group
+    counters); one per stream of concurrent calls."""
+    lib = _lib.load()
+    nbytes = int(lib.ps_b200_qkv_proj_workspace_bytes(int(n_local), int(heads), int(head_dim)))
+    return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
+
+
+def _opt_ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _vector(t, n, name, device):
+    if t is None:
+        return None
+    if t.dim() != 1 or t.shape[0] != n or not t.is_contiguous() or t.device != device:
+        raise ValueError(f"{name}: expected a contiguous [{n}] tensor on {device}")
+    return t
+
+
+def qkv_projection(x, w_q, w_k, w_v, b_q, b_k, b_v, norm_q, norm_k, freqs, dst_blocks, geo: UlyssesGeometry,
+                   eps: float, workspace: torch.Tensor, status: DeviceStatus | None = None):
+    """q|k|v = x W^T + b with RMSNorm (full width), norm weights and RoPE on q/k,
+    stored straight into destination d's [3, width, h, D] block at the device
+    address ``dst_blocks[d]`` (a slice of the local send buffer or a peer's
+    receive buffer) - the projections plus the whole pre-pass in one kernel.
+
+    x [n_local, in_features] (unit inner stride), w_* [H*D, in_features]
+    contiguous (PyTorch Linear weights, x's dtype), b_* [H*D] or None,
+    norm_* [H*D] (fp32 or x's dtype), freqs [n_local, D/2, 2, 2] fp32."""
+    lib = _lib.load()
+    _check16(x, "projection x")
+    device, dtype = x.device, x.dtype
+    width = geo.heads * geo.head_dim
+    if x.dim() != 2 or x.shape[0] != geo.n_local or x.stride(1) != 1:
+        raise ValueError(f"projection x: expected [{geo.n_local}, in_features] with unit inner stride")
+    fin = x.shape[1]
+    for t, name in ((w_q, "w_q"), (w_k, "w_k"), (w_v, "w_v")):
+        if t.dtype != dtype or tuple(t.shape) != (width, fin) or not t.is_contiguous() or t.device != device:
+            raise ValueError(f"projection {name}: expected contiguous [{width}, {fin}] {dtype}")
+    biases = [_vector(b, width, f"b_{n}", device) for b, n in ((b_q, "q"), (b_k, "k"), (b_v, "v"))]
+    bdt = next((b.dtype for b in biases if b is not None), torch.float32)
+    if any(b is not None and b.dtype != bdt for b in biases):
+        raise ValueError("projection biases must share a dtype")
+    _vector(norm_q, width, "norm_q", device)
+    _vector(norm_k, width, "norm_k", device)
+    if norm_q.dtype != norm_k.dtype:
+        raise ValueError("projection norm weights must share a dtype")
+    if (freqs.dtype != torch.float32 or freqs.dim() != 4 or freqs.shape[0] != geo.n_local
+            or tuple(freqs.shape[1:]) != (geo.head_dim // 2, 2, 2) or freqs.stride()[1:] != (4, 2, 1)):
+        raise ValueError(f"projection freqs: expected [{geo.n_local}, {geo.head_dim // 2}, 2, 2] fp32")
+    if len(dst_blocks) != geo.world:
+        raise ValueError(f"projection: {len(dst_blocks)} destination blocks for {geo.world} ranks")
+    rc = lib.ps_b200_qkv_proj(
+        x.data_ptr(), x.stride(0), w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr(), *[_opt_ptr(b) for b in biases],
+        _lib.dtype_code(bdt), norm_q.data_ptr(), norm_k.data_ptr(), _lib.dtype_code(norm_q.dtype), freqs.data_ptr(),
+        freqs.stride(0), _lib.ptrs(dst_blocks), _lib.dtype_code(dtype), geo.world, geo.n_local, geo.width, geo.heads,
+        geo.heads_per_rank, geo.head_dim, fin, float(eps), *_ws(workspace),
+        status.ptr if status is not None else None, _lib.stream_handle(device))
+    _lib.check(rc, "ps_b200_qkv_proj")
+    if status is not None:
+        status.arm()
+
+
+def out_projection(src, w_o, b_o, out, n_local: int, in_features: int, row_stride: int, block_stride: int = 0,
+                   block_cols: int = 0, status: DeviceStatus | None = None):
+    """out = A W_o^T + b_o with A row i read in place from ``src`` (a tensor or
+    its storage): row i at element i*row_stride, or - with block_cols > 0 -
+    its columns [b*block_cols, (b+1)*block_cols) at b*block_stride +
+    i*row_stride (the NCCL receive buffer's per-source blocks)."""
+    lib = _lib.load()
+    _check16(src, "projection source")
+    _lib.require_cuda(out, "projection out")
+    dtype = src.dtype
+    fout = w_o.shape[0]
+    if w_o.dtype != dtype or tuple(w_o.shape) != (fout, in_features) or not w_o.is_contiguous():
+        raise ValueError(f"projection w_o: expected contiguous [out_features, {in_features}] {dtype}")
+    b_o = _vector(b_o, fout, "b_o", src.device)
+    if out.dim() != 2 or tuple(out.shape) != (n_local, fout) or out.stride(1) != 1 or out.dtype not in (
+            dtype, torch.float32):
+        raise ValueError(f"projection out: expected [{n_local}, {fout}] with unit inner stride")
+    rc = lib.ps_b200_out_proj(
+        src.data_ptr(), int(row_stride), int(block_stride), int(block_cols), w_o.data_ptr(), _opt_ptr(b_o),
+        _lib.dtype_code(b_o.dtype if b_o is not None else torch.float32), out.data_ptr(), out.stride(0),
+        _lib.dtype_code(dtype), _lib.dtype_code(out.dtype), int(n_local), int(in_features), int(fout),
+        status.ptr if status is not None else None, _lib.stream_handle(src.device))
+    _lib.check(rc, "ps_b200_out_proj")
+    if status is not None:
+        status.arm()

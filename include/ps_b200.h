@@ -43,6 +43,14 @@
  *                          all-gather; the broadcast all-gathers text outputs.
  *   ps_b200_prepass rope_style 1   rope_split_half of the H3 path,
  *                          powershard/attention.py:98-103.
+ *   ps_b200_qkv_proj       the q/k/v Linear layers of attention_qkv
+ *                          (wan_model.py:425-429, self.q/k/v) as one GEMM whose
+ *                          epilogue also does norm_q/norm_k, rope_apply and the
+ *                          send-side pack (the whole of ps_b200_prepass).
+ *   ps_b200_out_proj       self.o (wan_model.py:438) reading the attention
+ *                          output from the exchange buffer in place: the
+ *                          receive-side unpack of ulysses_to_heads
+ *                          (wan_model.py:377-380) fused into the GEMM.
  *   ps_b200_prepass_batch, ps_b200_ulysses_attn_batch, ps_b200_unpack_batch
  *                          the same three steps for a batch of rows (CFG) in
  *                          one exchange, as the reference packs it: send
@@ -340,6 +348,52 @@ int ps_b200_ulysses_attn_batch(const void* recv, void* const* out_blocks, int64_
 int ps_b200_unpack_batch(const void* recv, int64_t src_stride, int64_t batch_stride, int64_t row_stride, void* out,
                          int64_t out_batch_stride, int64_t out_row_stride, int dtype, int out_dtype, int batch,
                          int n_local, int heads, int heads_per_rank, int head_dim, void* stream);
+
+/*
+ * Projection GEMMs (tcgen05, one persistent CTA per SM, cooperative launch).
+ *
+ * ps_b200_qkv_proj: q|k|v = x [W_q|W_k|W_v]^T + b for this rank's n_local
+ *   tokens, x [n_local][in_features] (row stride x_row_stride), weights
+ *   [heads*head_dim][in_features] row-major (PyTorch Linear), biases b_*
+ *   [heads*head_dim] (b_dtype = dtype or FP32; NULL = none).  The q and k
+ *   outputs are RMS-normalised over the full width (eps, weights w_qnorm /
+ *   w_knorm), rotated by freqs [n_local][head_dim/2][2][2] and, with v, stored
+ *   as ps_b200_prepass_to stores them: dst_blocks[d] receives destination
+ *   d's [3][seg_rows][heads_per_rank][head_dim] block, padding rows and head
+ *   slots zeroed.  The projections themselves never reach memory.  The RMS
+ *   statistic is taken over the fp32 accumulator (not a rounded projection).
+ *   head_dim 128, heads even, in_features % 64 == 0.  workspace: device
+ *   scratch of ps_b200_qkv_proj_workspace_bytes(n_local, heads, head_dim)
+ *   bytes (per-row partial sums of squares and group counters), owned by one
+ *   call at a time.  status: device int (may be NULL) receiving a
+ *   PS_B200_DEVICE_TIMEOUT_* code if a bounded wait expires.
+ */
+size_t ps_b200_qkv_proj_workspace_bytes(int n_local, int heads, int head_dim);
+int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const void* w_k, const void* w_v,
+                     const void* b_q, const void* b_k, const void* b_v, int b_dtype, const void* w_qnorm,
+                     const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_row_stride,
+                     void* const* dst_blocks, int dtype, int world, int n_local, int seg_rows, int heads,
+                     int heads_per_rank, int head_dim, int in_features, float eps, void* workspace,
+                     size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * ps_b200_out_proj: out = A W_o^T + b_o, out [n_local][out_features]
+ *   (out_dtype = dtype or FP32, row stride out_row_stride), W_o
+ *   [out_features][in_features].  A row i is read in place from the
+ *   exchange buffer that holds the attention output:
+ *     src_block_cols == 0: src row i at src + i*src_row_stride (the peer
+ *       exchange's staging buffer [seg_rows][world*h][head_dim]: row stride
+ *       world*h*head_dim, its first heads*head_dim columns are the heads in
+ *       order);
+ *     src_block_cols > 0: columns [b*src_block_cols, (b+1)*src_block_cols) of
+ *       row i at src + b*src_block_stride + i*src_row_stride (the NCCL
+ *       receive buffer [world][seg_rows][h][head_dim]: block stride
+ *       seg_rows*h*head_dim, row stride and block width h*head_dim).
+ *   in_features % 64 == 0, out_features % 256 == 0, 16-byte aligned buffers.
+ */
+int ps_b200_out_proj(const void* src, int64_t src_row_stride, int64_t src_block_stride, int src_block_cols,
+                     const void* w_o, const void* b_o, int b_dtype, void* out, int64_t out_row_stride, int dtype,
+                     int out_dtype, int n_local, int in_features, int out_features, int* status, void* stream);
 
 /*
  * Self-test of the bounded waits (no counterpart in the reference): one warp
