@@ -761,10 +761,10 @@ int64_t qkv_rows_blocks(int n) { return (int64_t(n) + 127) / 128; }
 
 extern "C" {
 
-size_t ps_b200_qkv_proj_workspace_bytes(int n_local, int heads, int head_dim) {
-  if (n_local <= 0 || heads <= 0 || head_dim <= 0) return 0;
+size_t ps_b200_qkv_proj_workspace_bytes(int rows, int heads, int head_dim) {
+  if (rows <= 0 || heads <= 0 || head_dim <= 0) return 0;
   const int64_t width = int64_t(heads) * head_dim;
-  const int64_t groups = 2 * psb::qkv_rows_blocks(n_local);
+  const int64_t groups = 2 * psb::qkv_rows_blocks(rows);
   const int64_t part = groups * (width / 256) * 128 * 4;
   return static_cast<size_t>(((part + 255) / 256) * 256 + ((groups * 4 + 255) / 256) * 256);
 }
@@ -775,11 +775,25 @@ int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const
                      void* const* dst_blocks, int dtype, int world, int n_local, int seg_rows, int heads,
                      int heads_per_rank, int head_dim, int in_features, float eps, void* workspace,
                      size_t workspace_bytes, int* status, void* stream) {
+  return ps_b200_qkv_proj_batch(x, x_row_stride, w_q, w_k, w_v, b_q, b_k, b_v, b_dtype, w_qnorm, w_knorm, w_dtype,
+                                freqs, 0, freqs_row_stride, dst_blocks, dtype, 1, world, n_local, seg_rows, heads,
+                                heads_per_rank, head_dim, in_features, eps, workspace, workspace_bytes, status,
+                                stream);
+}
+
+int ps_b200_qkv_proj_batch(const void* x, int64_t x_row_stride, const void* w_q, const void* w_k, const void* w_v,
+                           const void* b_q, const void* b_k, const void* b_v, int b_dtype, const void* w_qnorm,
+                           const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_batch_stride,
+                           int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int batch, int world,
+                           int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, int in_features,
+                           float eps, void* workspace, size_t workspace_bytes, int* status, void* stream) {
   using namespace psb;
   if (!is16bit(dtype)) return set_error(PS_B200_ERR_UNSUPPORTED, "projection supports bf16 and fp16 only");
   if (world < 1 || world > kMaxSegs || n_local < 0 || seg_rows < n_local || heads < 1 || heads_per_rank < 1 ||
-      int64_t(heads_per_rank) * world < heads || in_features <= 0)
+      int64_t(heads_per_rank) * world < heads || in_features <= 0 || batch < 0 || freqs_batch_stride < 0 ||
+      freqs_batch_stride % 4 != 0)
     return set_error(PS_B200_ERR_INVALID, "inconsistent projection geometry");
+  if (int64_t(batch) * n_local >= (int64_t(1) << 31)) return set_error(PS_B200_ERR_UNSUPPORTED, "too many rows");
   if (head_dim != 128) return set_error(PS_B200_ERR_UNSUPPORTED, "projection supports head_dim 128 only");
   const int64_t width = int64_t(heads) * head_dim;
   if (width % 256 != 0) return set_error(PS_B200_ERR_UNSUPPORTED, "projection needs an even head count");
@@ -787,17 +801,20 @@ int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const
   if (b_dtype != dtype && b_dtype != PS_B200_FP32) return set_error(PS_B200_ERR_UNSUPPORTED, "bias dtype");
   if (w_dtype != dtype && w_dtype != PS_B200_FP32) return set_error(PS_B200_ERR_UNSUPPORTED, "norm weight dtype");
   if (!std::isfinite(eps) || eps < 0.f) return set_error(PS_B200_ERR_INVALID, "eps must be finite and >= 0");
-  if (seg_rows == 0) return PS_B200_OK;
+  if (seg_rows == 0 || batch == 0) return PS_B200_OK;
   if (!dst_blocks) return set_error(PS_B200_ERR_INVALID, "null destination table");
   for (int d = 0; d < world; ++d)
     if (!dst_blocks[d] || !aligned16(dst_blocks[d]))
       return set_error(PS_B200_ERR_INVALID, "destination block %d null or not 16-byte aligned", d);
   ProjArgs a{};
-  a.n = n_local;
+  a.n = batch * n_local;
+  a.batch = batch;
+  a.n_local = n_local;
+  a.freqs_batch_stride = batch > 1 ? freqs_batch_stride : 0;
   a.kdim = in_features;
   a.width = static_cast<int>(width);
   a.ntile_n = static_cast<int>(width / 256);
-  a.row_blocks = static_cast<int>(qkv_rows_blocks(n_local));
+  a.row_blocks = static_cast<int>(qkv_rows_blocks(a.n));
   a.epi = 1;
   a.bias[0] = b_q;
   a.bias[1] = b_k;
@@ -816,14 +833,14 @@ int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const
   a.heads_per_rank = heads_per_rank;
   a.head_dim = head_dim;
   a.status = status;
-  if (n_local > 0) {
+  if (a.n > 0) {
     if (!x || !w_q || !w_k || !w_v || !w_qnorm || !w_knorm || !freqs || !aligned16(x) || !aligned16(w_q) ||
         !aligned16(w_k) || !aligned16(w_v) || !aligned16(w_qnorm) || !aligned16(w_knorm) || !aligned16(freqs) ||
         freqs_row_stride % 4 != 0 || freqs_row_stride < head_dim * 2)
       return set_error(PS_B200_ERR_INVALID, "projection inputs must be non-null and 16-byte aligned");
     for (const void* b : {b_q, b_k, b_v})
       if (b && !aligned16(b)) return set_error(PS_B200_ERR_INVALID, "bias must be 16-byte aligned");
-    const size_t need = ps_b200_qkv_proj_workspace_bytes(n_local, heads, head_dim);
+    const size_t need = ps_b200_qkv_proj_workspace_bytes(a.n, heads, head_dim);
     if (!workspace || workspace_bytes < need || !aligned16(workspace))
       return set_error(PS_B200_ERR_INVALID, "projection workspace of %zu bytes required", need);
     if (int rc = check_device()) return rc;
@@ -845,7 +862,7 @@ int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const
     if (err != cudaSuccess) return set_cuda_error("projection: clearing the group counters", err);
     const bool fp16 = dtype == PS_B200_FP16;
     CUtensorMap ta, tw[3];
-    if (int rc = make_map_2d(&ta, x, fp16, in_features, n_local, x_row_stride, 128)) return rc;
+    if (int rc = make_map_2d(&ta, x, fp16, in_features, a.n, x_row_stride, 128)) return rc;
     const void* ws[3] = {w_q, w_k, w_v};
     for (int i = 0; i < 3; ++i)
       if (int rc = make_map_2d(&tw[i], ws[i], fp16, in_features, width, in_features, 256)) return rc;

@@ -100,7 +100,10 @@ int launch_unpack(const UnpackArgs& a, bool fp16, cudaStream_t stream);
 
 // Arguments of the projection GEMMs (proj.cu) that are not tensor maps.
 struct ProjArgs {
-  int n;                   // rows of A (this rank's tokens)
+  int n;                   // rows of A: batch * n_local (epi 1) or this rank's tokens (epi 0)
+  int batch;               // epi 1: batch rows; GEMM row m is token m % n_local of batch row m / n_local
+  int n_local;             // epi 1: tokens per batch row
+  int64_t freqs_batch_stride;  // epi 1: floats between the rotation tables of batch rows (0: shared)
   int kdim;                // K: input features (a multiple of 64)
   int width;               // output features of one projection (a multiple of 256)
   int ntile_n;             // width / 256: column tiles of one projection
@@ -115,7 +118,7 @@ struct ProjArgs {
   const float* freqs;      // [n][head_dim/2][2][2] rotation table
   int64_t freqs_row_stride;
   float eps;
-  void* dst[kMaxSegs];     // epi 1: destination d's block [3][seg_rows][heads_per_rank][head_dim]
+  void* dst[kMaxSegs];     // epi 1: destination d's block [3][batch][seg_rows][heads_per_rank][head_dim]
   int world, seg_rows, heads, heads_per_rank, head_dim;
   void* out;               // epi 0: [n][width] (row stride out_row_stride elements)
   int64_t out_row_stride;

@@ -333,8 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = warp_wait(bar(kAccFull + b), ((seq - 1) >> 1) & 1u, abort_flag, status, kErrAcc);
       tc_fence_after();
       const uint32_t acc = tmem + lane_off + b * kBN;
-      const int token = t.rb * kBM + row;
-      const bool live = token < a.n;
+      const int m = t.rb * kBM + row;  // GEMM row
+      const bool live = m < a.n;
+      // epi 1: batch row and token of GEMM row m; epi 0: the token itself.
+      const int bi = a.epi == 1 ? m / a.n_local : 0;
+      const int token = a.epi == 1 ? m - bi * a.n_local : m;
       const int n0 = t.tile * kBN;
       const void* bias = a.bias[t.kind];
       if (a.epi == 0) {
@@ -413,7 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Pass 2: (q/k) normalise, weight, rotate; store to the send layout.
         if (ok) {
           const void* nw = t.kind < 2 ? a.normw[t.kind] : nullptr;
-          const float* frow = a.freqs + static_cast<int64_t>(live ? token : 0) * a.freqs_row_stride;
+          const float* frow = a.freqs + (live ? bi * a.freqs_batch_stride + static_cast<int64_t>(token) *
+                                                                                  a.freqs_row_stride : 0);
 #pragma unroll 1
           for (int ch = 0; ch < kBN / 32; ++ch) {
             uint32_t v[32];
@@ -451,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int dest = g / h;
               const int slot = g - dest * h;
               uint16_t* dst = static_cast<uint16_t*>(a.dst[dest]) +
-                              ((static_cast<int64_t>(t.kind) * a.seg_rows + token) * h + slot) * D + d0;
+                              (((static_cast<int64_t>(t.kind) * a.batch + bi) * a.seg_rows + token) * h + slot) * D + d0;
               store32_16<kFp16>(dst, y);
             }
           }
@@ -471,24 +475,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Zero padding of the send layout: token rows [n, seg_rows) of every slot and
-// head slots [heads, world * h) of rows [0, n), for the three kinds.
+// Zero padding of the send layout: token rows [n_local, seg_rows) of every
+// slot and head slots [heads, world * h) of rows [0, n_local), for the three
+// kinds and every batch row.
 __global__ void __launch_bounds__(256) pad_kernel(const ProjArgs a) {
   const int D = a.head_dim, h = a.heads_per_rank;
   const int vph = D / 8;
   const int64_t slots_per_row = static_cast<int64_t>(a.world) * h;
-  const int64_t pad_rows = static_cast<int64_t>(a.seg_rows - a.n) * slots_per_row;  // padding rows, all slots
-  const int64_t pad_heads = static_cast<int64_t>(a.n) * (slots_per_row - a.heads);  // padded slots of live rows
-  const int64_t per_kind = (pad_rows + pad_heads) * vph;
-  const int64_t total = 3 * per_kind;
+  const int64_t pad_rows = static_cast<int64_t>(a.seg_rows - a.n_local) * slots_per_row;  // padding rows, all slots
+  const int64_t pad_heads = static_cast<int64_t>(a.n_local) * (slots_per_row - a.heads);  // padded slots of live rows
+  const int64_t per_kb = (pad_rows + pad_heads) * vph;  // one (kind, batch row)
+  const int64_t total = 3 * static_cast<int64_t>(a.batch) * per_kb;
   for (int64_t v = blockIdx.x * 256ll + threadIdx.x; v < total; v += static_cast<int64_t>(gridDim.x) * 256) {
-    const int kind = static_cast<int>(v / per_kind);
-    int64_t u = v - kind * per_kind;
+    const int64_t kb = v / per_kb;  // kind * batch + b
+    int64_t u = v - kb * per_kb;
     const int dd = static_cast<int>(u % vph) * 8;
     u /= vph;
     int token, g;
     if (u < pad_rows) {
-      token = a.n + static_cast<int>(u / slots_per_row);
+      token = a.n_local + static_cast<int>(u / slots_per_row);
       g = static_cast<int>(u % slots_per_row);
     } else {
       u -= pad_rows;
@@ -498,8 +503,7 @@ __global__ void __launch_bounds__(256) pad_kernel(const ProjArgs a) {
     }
     const int dest = g / h;
     const int slot = g - dest * h;
-    uint16_t* dst = static_cast<uint16_t*>(a.dst[dest]) +
-                    ((static_cast<int64_t>(kind) * a.seg_rows + token) * h + slot) * D + dd;
+    uint16_t* dst = static_cast<uint16_t*>(a.dst[dest]) + ((kb * a.seg_rows + token) * h + slot) * D + dd;
     *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
@@ -525,10 +529,10 @@ int launch_proj(const CUtensorMap& ta, const CUtensorMap& tw0, const CUtensorMap
                 const ProjArgs& args, bool fp16, int ctas, cudaStream_t stream) {
   using namespace proj;
   if (args.epi == 1) {
-    const int64_t pads = (static_cast<int64_t>(args.seg_rows - args.n) * args.world * args.heads_per_rank +
-                          static_cast<int64_t>(args.n) * (args.world * args.heads_per_rank - args.heads));
+    const int64_t pads = (static_cast<int64_t>(args.seg_rows - args.n_local) * args.world * args.heads_per_rank +
+                          static_cast<int64_t>(args.n_local) * (args.world * args.heads_per_rank - args.heads));
     if (pads > 0) {
-      const int64_t vecs = 3 * pads * (args.head_dim / 8);
+      const int64_t vecs = 3 * int64_t(args.batch) * pads * (args.head_dim / 8);
       const int blocks = static_cast<int>(vecs / 256 + 1 < 4096 ? vecs / 256 + 1 : 4096);
       pad_kernel<<<blocks, 256, 0, stream>>>(args);
       cudaError_t err = cudaGetLastError();

@@ -535,11 +535,12 @@ def attention_blhd(q, k, v, out, scale: float, status: DeviceStatus | None, work
 
 
 # ------------------------------------------------------------ projection GEMMs
-def projection_workspace(n_local: int, heads: int, head_dim: int, device: torch.device) -> torch.Tensor:
-    """Scratch of ``qkv_projection`` (per-row partial sums of squares and group
-    counters); one per stream of concurrent calls."""
+def projection_workspace(rows: int, heads: int, head_dim: int, device: torch.device) -> torch.Tensor:
+    """Scratch of ``qkv_projection`` for ``rows`` = batch * n_local rows (per-row
+    partial sums of squares and group counters); one per stream of
+    concurrent calls."""
     lib = _lib.load()
-    nbytes = int(lib.ps_b200_qkv_proj_workspace_bytes(int(n_local), int(heads), int(head_dim)))
+    nbytes = int(lib.ps_b200_qkv_proj_workspace_bytes(int(rows), int(heads), int(head_dim)))
     return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
 
 
@@ -558,20 +559,28 @@ def _vector(t, n, name, device):
 def qkv_projection(x, w_q, w_k, w_v, b_q, b_k, b_v, norm_q, norm_k, freqs, dst_blocks, geo: UlyssesGeometry,
                    eps: float, workspace: torch.Tensor, status: DeviceStatus | None = None):
     """q|k|v = x W^T + b with RMSNorm (full width), norm weights and RoPE on q/k,
-    stored straight into destination d's [3, width, h, D] block at the device
-    address ``dst_blocks[d]`` (a slice of the local send buffer or a peer's
-    receive buffer) - the projections plus the whole pre-pass in one kernel.
+    stored straight into destination d's block at the device address
+    ``dst_blocks[d]`` (a slice of the local send buffer or a peer's receive
+    buffer) - the projections plus the whole pre-pass in one kernel.
 
-    x [n_local, in_features] (unit inner stride), w_* [H*D, in_features]
+    x [n_local, in_features], or [B, n_local, in_features] for a batch of
+    rows in one GEMM (destination blocks [3, B, width, h, D]); unit inner
+    stride, batch rows one after the other.  w_* [H*D, in_features]
     contiguous (PyTorch Linear weights, x's dtype), b_* [H*D] or None,
-    norm_* [H*D] (fp32 or x's dtype), freqs [n_local, D/2, 2, 2] fp32."""
+    norm_* [H*D] (fp32 or x's dtype), freqs [n_local, D/2, 2, 2] fp32 (or
+    [B, n_local, D/2, 2, 2]).  workspace: ``projection_workspace(B * n_local, ...)``."""
     lib = _lib.load()
     _check16(x, "projection x")
     device, dtype = x.device, x.dtype
     width = geo.heads * geo.head_dim
-    if x.dim() != 2 or x.shape[0] != geo.n_local or x.stride(1) != 1:
-        raise ValueError(f"projection x: expected [{geo.n_local}, in_features] with unit inner stride")
-    fin = x.shape[1]
+    batch = x.shape[0] if x.dim() == 3 else 1
+    rows = x if x.dim() == 2 else x.reshape(batch * x.shape[1], x.shape[2])
+    if rows.shape[0] != batch * geo.n_local or rows.stride(-1) != 1 or (x.dim() == 3 and x.shape[1] != geo.n_local):
+        raise ValueError(f"projection x: expected [{geo.n_local}, in_features] or [B, {geo.n_local}, in_features] "
+                         "with unit inner stride and consecutive batch rows")
+    if x.dim() == 3 and batch > 1 and x.stride(0) != geo.n_local * x.stride(1):
+        raise ValueError("projection x: batch rows must follow each other")
+    fin = rows.shape[1]
     for t, name in ((w_q, "w_q"), (w_k, "w_k"), (w_v, "w_v")):
         if t.dtype != dtype or tuple(t.shape) != (width, fin) or not t.is_contiguous() or t.device != device:
             raise ValueError(f"projection {name}: expected contiguous [{width}, {fin}] {dtype}")
@@ -583,18 +592,25 @@ def qkv_projection(x, w_q, w_k, w_v, b_q, b_k, b_v, norm_q, norm_k, freqs, dst_b
     _vector(norm_k, width, "norm_k", device)
     if norm_q.dtype != norm_k.dtype:
         raise ValueError("projection norm weights must share a dtype")
-    if (freqs.dtype != torch.float32 or freqs.dim() != 4 or freqs.shape[0] != geo.n_local
-            or tuple(freqs.shape[1:]) != (geo.head_dim // 2, 2, 2) or freqs.stride()[1:] != (4, 2, 1)):
+    fb = 0
+    table = freqs
+    if freqs.dim() == 5:
+        if freqs.shape[0] != batch:
+            raise ValueError(f"projection freqs: {freqs.shape[0]} tables for {batch} batch rows")
+        fb, table = freqs.stride(0), freqs[0]
+    if (table.dtype != torch.float32 or table.dim() != 4 or table.shape[0] != geo.n_local
+            or tuple(table.shape[1:]) != (geo.head_dim // 2, 2, 2) or table.stride()[1:] != (4, 2, 1)):
         raise ValueError(f"projection freqs: expected [{geo.n_local}, {geo.head_dim // 2}, 2, 2] fp32")
     if len(dst_blocks) != geo.world:
         raise ValueError(f"projection: {len(dst_blocks)} destination blocks for {geo.world} ranks")
-    rc = lib.ps_b200_qkv_proj(
-        x.data_ptr(), x.stride(0), w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr(), *[_opt_ptr(b) for b in biases],
-        _lib.dtype_code(bdt), norm_q.data_ptr(), norm_k.data_ptr(), _lib.dtype_code(norm_q.dtype), freqs.data_ptr(),
-        freqs.stride(0), _lib.ptrs(dst_blocks), _lib.dtype_code(dtype), geo.world, geo.n_local, geo.width, geo.heads,
-        geo.heads_per_rank, geo.head_dim, fin, float(eps), *_ws(workspace),
-        status.ptr if status is not None else None, _lib.stream_handle(device))
-    _lib.check(rc, "ps_b200_qkv_proj")
+    rc = lib.ps_b200_qkv_proj_batch(
+        rows.data_ptr(), rows.stride(0), w_q.data_ptr(), w_k.data_ptr(), w_v.data_ptr(),
+        *[_opt_ptr(b) for b in biases], _lib.dtype_code(bdt), norm_q.data_ptr(), norm_k.data_ptr(),
+        _lib.dtype_code(norm_q.dtype), table.data_ptr(), fb, table.stride(0), _lib.ptrs(dst_blocks),
+        _lib.dtype_code(dtype), batch, geo.world, geo.n_local, geo.width, geo.heads, geo.heads_per_rank,
+        geo.head_dim, fin, float(eps), *_ws(workspace), status.ptr if status is not None else None,
+        _lib.stream_handle(device))
+    _lib.check(rc, "ps_b200_qkv_proj_batch")
     if status is not None:
         status.arm()
 

@@ -202,6 +202,91 @@ class UlyssesAttention:
         self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local", batch)
         return out
 
+    def forward_layer(self, x, w_q, w_k, w_v, w_o, norm_q, norm_k, freqs, b_q=None, b_k=None, b_v=None, b_o=None,
+                      *, total: int, heads: int, eps: float = 1e-6, scale: float | None = None,
+                      out_dtype: torch.dtype | None = None, state: dict | None = None,
+                      local: bool = False) -> torch.Tensor:
+        """The whole self-attention layer of this rank's tokens in the fused
+        kernels: [B, n_local, in_features] -> [B, n_local, out_features].
+
+        The q/k/v projections, RMSNorm over the full width, RoPE and the
+        Ulysses pack run as one GEMM (``ps_b200_qkv_proj_batch``) whose
+        epilogue stores into the send layout or the peers' receive buffers;
+        then the exchange, attention and the inverse exchange as in
+        ``forward_batch``; the output projection (``ps_b200_out_proj``) reads
+        the attention output from the exchange buffer in place.  So neither
+        the projections nor the attention output make a separate round trip
+        through HBM (powershard/wan_model.py:425-438 in one pass).
+
+        x and the weights share the 16-bit wire type (w_* [H*D, in_features],
+        w_o [out_features, H*D], PyTorch Linear layout); biases [*] or None;
+        norm_* [H*D]; freqs [n_local, D/2, 2, 2] fp32 (or one table per batch
+        row).  Needs the CUDA kernels (head_dim 128, an even head count).
+        """
+        if self.kernels is not ops or x.device.type != "cuda":
+            raise RuntimeError("forward_layer runs on the CUDA kernels only")
+        device, dtype = x.device, x.dtype
+        batch, n, _ = x.shape
+        head_dim = w_q.shape[0] // heads
+        geo = self.geometry(total, heads, head_dim, local)
+        if n != geo.n_local:
+            raise ValueError("Ulysses local token/head geometry mismatch")
+        out_dtype = out_dtype or dtype
+        scale = head_dim ** -0.5 if scale is None else float(scale)
+        fout = w_o.shape[0]
+        hd = heads * head_dim
+        h = geo.heads_per_rank
+        out = torch.empty((batch, n, fout), dtype=out_dtype, device=device)
+        if batch == 0:
+            return out
+        x = x if x.is_contiguous() else x.contiguous()
+        with torch.cuda.device(device):
+            status = self._device_status(device)
+            status.poll()
+            pws = self._proj_workspace(device, batch * n, heads, head_dim)
+            px = self._peer(geo, dtype, device, batch=batch)
+            if px is not None:
+                ops.qkv_projection(x, w_q, w_k, w_v, b_q, b_k, b_v, norm_q, norm_k, freqs, px.dst_blocks, geo, eps,
+                                   pws, status)
+                px.barrier()
+                ops.ulysses_attention_to(px.recv, px.out_blocks, px.out_row_stride, dtype, geo, scale, status,
+                                         **self._ws(device), batch=batch, out_batch_stride=px.out_batch_stride)
+                px.barrier()
+                for b in range(batch):  # staging rows [width][W*h][D]: the first H*D columns in head order
+                    ops.out_projection(px.staging[b], w_o, b_o, out[b], n, hd, geo.padded_heads * head_dim,
+                                       status=status)
+                self._count(state, geo, dtype, "peer", batch)
+                return out
+            ws, _ = self._workspace(geo, dtype, device, batch)
+            ops.qkv_projection(x, w_q, w_k, w_v, b_q, b_k, b_v, norm_q, norm_k, freqs, ops.send_blocks(ws["send"]),
+                               geo, eps, pws, status)
+            self._exchange(ws["recv"], ws["send"], geo)
+            if geo.world == 1:
+                key = ("attn_out", device.index, torch.cuda.current_stream(device).cuda_stream, batch, n, hd, dtype)
+                attn = self._buffers.get(key)
+                if attn is None:
+                    attn = self._buffers[key] = torch.empty((batch, n, heads, head_dim), dtype=dtype, device=device)
+                ops.ulysses_attention(ws["recv"], attn.view(1, batch, n, heads, head_dim), geo, scale, status,
+                                      **self._ws(device))
+                for b in range(batch):
+                    ops.out_projection(attn[b], w_o, b_o, out[b], n, hd, hd, status=status)
+            else:
+                ops.ulysses_attention(ws["recv"], ws["out_send"], geo, scale, status, **self._ws(device))
+                self._exchange(ws["out_recv"], ws["out_send"], geo)
+                for b in range(batch):  # receive blocks [W][B][width][h][D]: heads of source s in block s
+                    ops.out_projection(ws["out_recv"][0, b], w_o, b_o, out[b], n, hd, h * head_dim,
+                                       block_stride=batch * geo.width * h * head_dim, block_cols=h * head_dim,
+                                       status=status)
+        self._count(state, geo, dtype, "nccl" if geo.world > 1 else "local", batch)
+        return out
+
+    def _proj_workspace(self, device, rows: int, heads: int, head_dim: int):
+        key = ("proj_ws", device.index, torch.cuda.current_stream(device).cuda_stream, rows, heads, head_dim)
+        ws = self._buffers.get(key)
+        if ws is None:
+            ws = self._buffers[key] = ops.projection_workspace(rows, heads, head_dim, device)
+        return ws
+
     def _ws(self, device) -> dict:
         """Keyword argument with the attention workspace of (device, stream)
         for the CUDA kernels; stand-in kernels take none."""

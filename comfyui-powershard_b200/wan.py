@@ -1,9 +1,12 @@
 """Wan self-attention entry points with the PowerShard signatures.
 
 * ``self_attention_forward(self, x, freqs, transformer_options=None)`` -
-  replacement for powershard/wan_model.py:433-438.  Projections stay torch
-  Linear layers; q/k RMSNorm + RoPE run fused with the Ulysses pack in one
-  kernel, attention and unpack in the b200 kernels.
+  replacement for powershard/wan_model.py:433-438.  When q/k/v/o are plain
+  Linear layers (the reference's Linear without its scaled-fp16 path) the
+  whole layer runs in the fused kernels (``UlyssesAttention.forward_layer``:
+  q/k/v GEMM with RMSNorm + RoPE + pack in its epilogue, attention, output
+  GEMM reading the exchange buffer); otherwise the projections stay the
+  module's own layers and q/k RMSNorm + RoPE run fused with the pack.
 * ``sequence_attention(self, q, k, v, total=None)`` - replacement for
   powershard/wan_model.py:441-502 for callers that already produced
   normalised, rotated q/k (the pre-pass then only packs).
@@ -28,6 +31,7 @@ import types
 import torch
 import torch.distributed as dist
 
+from . import ops
 from .contract import AttentionOptions, UnsupportedAttention
 from .partition import shard_bounds
 from .ulysses import UlyssesAttention
@@ -87,6 +91,40 @@ def _run(engine, state, q, k, v, w_q, w_k, table, total, heads, norm_rope, out_d
     return torch.stack(outs)
 
 
+def _plain_linear(lin) -> bool:
+    """A Linear layer whose forward is x W^T + b: torch's, or the reference's
+    operations.Linear outside its scaled-fp16 / prepared-int8 paths."""
+    return (isinstance(lin, torch.nn.Linear) and not getattr(lin, "_ps_safe", False)
+            and getattr(lin, "_ps_prepared", None) is None and lin.weight.dim() == 2)
+
+
+def _fused_layers(module, dtype):
+    """(w_q, w_k, w_v, w_o, b_q, b_k, b_v, b_o) for the fused layer in the wire
+    dtype (weights cast once and cached while the parameters stay the same),
+    or None when the layer shape or the Linear layers do not fit it."""
+    if not getattr(module, "_ps_b200_fused_projections", True):
+        return None
+    lins = [getattr(module, name, None) for name in "qkvo"]
+    if not all(_plain_linear(lin) and lin.weight.is_cuda for lin in lins):
+        return None
+    heads, dim = module.num_heads, module.head_dim
+    width = heads * dim
+    fin = lins[0].weight.shape[1]
+    if (dim != 128 or width % 256 or fin % 64 or lins[3].weight.shape[0] % 256 or lins[3].weight.shape[1] != width
+            or any(tuple(lin.weight.shape) != (width, fin) for lin in lins[:3])):
+        return None
+    key = tuple((lin.weight.data_ptr(), lin.weight._version,
+                 None if lin.bias is None else (lin.bias.data_ptr(), lin.bias._version)) for lin in lins) + (dtype,)
+    cached = getattr(module, "_ps_b200_fused_cache", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    weights = [lin.weight.detach().to(dtype).contiguous() for lin in lins]
+    biases = [None if lin.bias is None else lin.bias.detach().float().contiguous() for lin in lins]
+    value = (*weights, *biases)
+    module._ps_b200_fused_cache = (key, value)
+    return value
+
+
 def self_attention_forward(self, x, freqs, transformer_options=None):
     """x [B, n, dim] -> [B, n, dim] through the fused Ulysses path (the whole
     batch in one exchange, as the reference)."""
@@ -106,6 +144,15 @@ def self_attention_forward(self, x, freqs, transformer_options=None):
     if w_q.dtype not in (torch.float32, WIRE_DTYPE):
         w_q, w_k = w_q.float(), w_k.float()
     eps = self.norm_q.eps if self.norm_q.eps is not None else 1e-6
+    token = state.get("enabled") and not state.get("ulysses", True)
+    fused = None if token or not x.is_cuda or engine.kernels is not ops else _fused_layers(self, WIRE_DTYPE)
+    if fused is not None:
+        # The whole layer in the fused kernels: no projection or attention
+        # output makes a separate round trip through memory.
+        out_dtype = x.dtype if x.is_floating_point() else WIRE_DTYPE
+        return engine.forward_layer(x.to(WIRE_DTYPE), *fused[:4], w_q.contiguous(), w_k.contiguous(), table,
+                                    *fused[4:], total=total, heads=heads, eps=eps, out_dtype=out_dtype,
+                                    state=state if state.get("enabled") else None, local=not state.get("enabled"))
     q_lin, k_lin, v_lin = self.q(x), self.k(x), self.v(x)
     out = _run(engine, state, _rows(q_lin, heads, dim, WIRE_DTYPE), _rows(k_lin, heads, dim, WIRE_DTYPE),
                _rows(v_lin, heads, dim, WIRE_DTYPE), w_q.contiguous(), w_k.contiguous(), table, total, heads,

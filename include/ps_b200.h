@@ -363,18 +363,33 @@ int ps_b200_unpack_batch(const void* recv, int64_t src_stride, int64_t batch_str
  *   slots zeroed.  The projections themselves never reach memory.  The RMS
  *   statistic is taken over the fp32 accumulator (not a rounded projection).
  *   head_dim 128, heads even, in_features % 64 == 0.  workspace: device
- *   scratch of ps_b200_qkv_proj_workspace_bytes(n_local, heads, head_dim)
+ *   scratch of ps_b200_qkv_proj_workspace_bytes(batch * n_local, heads, head_dim)
  *   bytes (per-row partial sums of squares and group counters), owned by one
  *   call at a time.  status: device int (may be NULL) receiving a
  *   PS_B200_DEVICE_TIMEOUT_* code if a bounded wait expires.
  */
-size_t ps_b200_qkv_proj_workspace_bytes(int n_local, int heads, int head_dim);
+size_t ps_b200_qkv_proj_workspace_bytes(int rows, int heads, int head_dim);
 int ps_b200_qkv_proj(const void* x, int64_t x_row_stride, const void* w_q, const void* w_k, const void* w_v,
                      const void* b_q, const void* b_k, const void* b_v, int b_dtype, const void* w_qnorm,
                      const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_row_stride,
                      void* const* dst_blocks, int dtype, int world, int n_local, int seg_rows, int heads,
                      int heads_per_rank, int head_dim, int in_features, float eps, void* workspace,
                      size_t workspace_bytes, int* status, void* stream);
+
+/*
+ * ps_b200_qkv_proj_batch: ps_b200_qkv_proj for a batch of rows (CFG) in one
+ *   GEMM: x holds batch * n_local rows (batch row b's tokens at rows
+ *   b*n_local ...), the rotation table of batch row b at freqs +
+ *   b*freqs_batch_stride floats (0: one table), and destination d's block is
+ *   [3][batch][seg_rows][heads_per_rank][head_dim] (the batched send layout of
+ *   ps_b200_prepass_batch).  ps_b200_qkv_proj is the case batch = 1.
+ */
+int ps_b200_qkv_proj_batch(const void* x, int64_t x_row_stride, const void* w_q, const void* w_k, const void* w_v,
+                           const void* b_q, const void* b_k, const void* b_v, int b_dtype, const void* w_qnorm,
+                           const void* w_knorm, int w_dtype, const float* freqs, int64_t freqs_batch_stride,
+                           int64_t freqs_row_stride, void* const* dst_blocks, int dtype, int batch, int world,
+                           int n_local, int seg_rows, int heads, int heads_per_rank, int head_dim, int in_features,
+                           float eps, void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /*
  * ps_b200_out_proj: out = A W_o^T + b_o, out [n_local][out_features]
