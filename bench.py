@@ -37,7 +37,10 @@ Outside the timed regions every rank also reports:
           tensors this rank's attention kernel reads, timed the same way;
   comm    (N > 1) bytes each rank sends across NVLink per step and what each
           exchange costs: the peer stores of the fused kernels against the
-          same kernels storing locally, and NCCL all_to_all_single.
+          same kernels storing locally, and NCCL all_to_all_single;
+  layer   the whole layer with its q/k/v/o projections: the fused tcgen05
+          GEMMs (forward_layer) against cuBLAS matmuls around the same
+          attention path, and each projection GEMM alone.
 """
 from __future__ import annotations
 
@@ -73,6 +76,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-layer", action="store_true", help="skip the whole-layer (projection GEMMs) report")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline work")
     p.add_argument("--profile", action="store_true",
                    help="ncu mode: profiler range around the timed steps only; no e2e / CPU baseline")
@@ -413,6 +417,86 @@ def measure_comm(engine, proj, norm_w, freqs, geo, dev, ms_step, attn_ms):
     return res
 
 
+def measure_layer(engine, geo, freqs, dev, world, reps=5):
+    """The whole self-attention layer (powershard/wan_model.py:421-438) of the
+    configs[1] shape, outside the headline timing: x [1, n, 5120] bf16 and
+    random bf16 q/k/v/o weights.  fused = UlyssesAttention.forward_layer (the
+    q/k/v GEMM with RMSNorm + RoPE + pack in its epilogue, exchange,
+    attention, output GEMM reading the exchange buffer); cublas = torch
+    matmuls for the four projections around the same attention path
+    (engine.forward).  Per-launch times of the projection GEMMs come from
+    CUDA events around each launch; every time is the max over ranks."""
+    from powershard_b200 import ops
+    n, total = geo.n_local, geo.total
+    g = torch.Generator(device=dev).manual_seed(2000 + geo.rank)
+    x = torch.randn(1, n, HIDDEN, device=dev, dtype=torch.bfloat16, generator=g)
+    ws = [(torch.randn(HIDDEN, HIDDEN, device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(4)]
+    norm = torch.ones(HIDDEN, device=dev, dtype=torch.float32)
+    kw = dict(total=total, heads=HEADS, local=world == 1)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    def fused():
+        return engine.forward_layer(x, *ws, norm, norm, freqs, **kw)
+
+    def cublas():
+        q, k, v = (x[0] @ w.t() for w in ws[:3])
+        o = engine.forward(q, k, v, norm, norm, freqs, **kw)
+        return o.view(n, HIDDEN) @ ws[3].t()
+
+    events = {"qkv_projection": [], "out_projection": []}
+    orig = {name: getattr(ops, name) for name in events}
+
+    def timed(name):
+        def run(*a_, **k_):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig[name](*a_, **k_)
+            e.record()
+            events[name].append((s, e))
+        return run
+
+    sync_all()
+    t_cublas = time_events(cublas, reps)
+    sync_all()
+    for name in events:
+        setattr(ops, name, timed(name))
+    try:
+        t_fused = time_events(fused, reps)
+    finally:
+        for name, fn in orig.items():
+            setattr(ops, name, fn)
+    sync_all()
+    t_gemm_qkv = time_events(lambda: [x[0] @ w.t() for w in ws[:3]], reps)
+    t_gemm_o = time_events(lambda: x[0] @ ws[3].t(), reps)
+    engine.check()
+    per = {k: statistics.mean(s.elapsed_time(e) for s, e in v[2:]) for k, v in events.items()}
+    vals = torch.tensor([t_fused, t_cublas, per["qkv_projection"], per["out_projection"], t_gemm_qkv, t_gemm_o],
+                        device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    t_fused, t_cublas, t_qkv, t_o, t_gemm_qkv, t_gemm_o = vals.tolist()
+    attn_flops = 4.0 * total * total * HEADS * DIM
+    proj_flops = 2.0 * total * HIDDEN * HIDDEN * 4          # the whole layer's four projections
+    del x, ws
+    tf = lambda flops, ms: flops / (ms * 1e-3) / 1e12  # noqa: E731
+    return dict(
+        fused_ms=t_fused, cublas_ms=t_cublas, fused_over_cublas_time=t_fused / t_cublas,
+        layer_tflops_fused=tf(attn_flops + proj_flops, t_fused),
+        layer_tflops_cublas=tf(attn_flops + proj_flops, t_cublas),
+        qkv_gemm_ms=t_qkv, qkv_gemm_tflops=tf(6.0 * n * HIDDEN * HIDDEN, t_qkv),
+        qkv_cublas_ms=t_gemm_qkv, qkv_cublas_tflops=tf(6.0 * n * HIDDEN * HIDDEN, t_gemm_qkv),
+        out_gemm_ms=t_o, out_gemm_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_o),
+        out_cublas_ms=t_gemm_o, out_cublas_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_gemm_o),
+        what="whole layer, x [1, n_local, 5120] bf16 -> [1, n_local, 5120]: fused = forward_layer (qkv GEMM with "
+             "RMSNorm/RoPE/pack epilogue, exchange, attention, o GEMM from the exchange buffer); cublas = torch "
+             "matmuls + engine.forward (pre-pass, exchange, attention, unpack); *_gemm = the fused GEMM kernels "
+             "alone (events around each launch), *_cublas = torch matmuls of the same shapes (q/k/v: three)")
+
+
 def workload_config(world, total=TOTAL):
     name = "Wan2.2-A14B self-attention block (configs[1])" if total == TOTAL else f"Wan-14B block, L={total}"
     return dict(workload=name, seq_len=total, heads=HEADS,
@@ -597,6 +681,8 @@ def main():
                 what="torch scaled_dot_product_attention on this rank's post-exchange q/k/v [1, h, L, 128] bf16, "
                      "CUDA events, max over ranks")
     comm = measure_comm(engine, proj, norm_w, freqs, geo, dev, ms, attn_ms) if world > 1 else None
+    del proj
+    layer = None if args.no_layer else measure_layer(engine, geo, freqs, dev, world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -619,7 +705,7 @@ def main():
             roofline=dict(bound="tensor", achieved=achieved, peak=peak, unit="TFLOP/s", frac=achieved / peak,
                           traffic=traffic, traffic_source=TRAFFIC_SOURCE, kernel="attn_fwd_kernel",
                           attn_ms_per_launch=attn_ms, flops_per_launch=attn_flops, peak_source=peak_src),
-            parity=parity, sdpa=sdpa, comm=comm,
+            parity=parity, sdpa=sdpa, comm=comm, layer=layer,
             cpu_baseline=cpu,
             e2e=dict(value=flops / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,
                      h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,

@@ -99,13 +99,15 @@ def _plain_linear(lin) -> bool:
 
 
 def _fused_layers(module, dtype):
-    """(w_q, w_k, w_v, w_o, b_q, b_k, b_v, b_o) for the fused layer in the wire
-    dtype (weights cast once and cached while the parameters stay the same),
-    or None when the layer shape or the Linear layers do not fit it."""
+    """(w_q, w_k, w_v, w_o, b_q, b_k, b_v, b_o) for the fused layer, or None
+    when the layer shape or the Linear layers do not fit it.  The weights
+    must already be in the wire dtype: a 16-bit Linear casts its input to its
+    weight dtype, as the fused GEMM does, while layers kept in fp32 keep their
+    own fp32 projections (the fused path never lowers their precision)."""
     if not getattr(module, "_ps_b200_fused_projections", True):
         return None
     lins = [getattr(module, name, None) for name in "qkvo"]
-    if not all(_plain_linear(lin) and lin.weight.is_cuda for lin in lins):
+    if not all(_plain_linear(lin) and lin.weight.is_cuda and lin.weight.dtype == dtype for lin in lins):
         return None
     heads, dim = module.num_heads, module.head_dim
     width = heads * dim
@@ -118,7 +120,7 @@ def _fused_layers(module, dtype):
     cached = getattr(module, "_ps_b200_fused_cache", None)
     if cached is not None and cached[0] == key:
         return cached[1]
-    weights = [lin.weight.detach().to(dtype).contiguous() for lin in lins]
+    weights = [lin.weight.detach().contiguous() for lin in lins]
     biases = [None if lin.bias is None else lin.bias.detach().float().contiguous() for lin in lins]
     value = (*weights, *biases)
     module._ps_b200_fused_cache = (key, value)

@@ -94,7 +94,7 @@ def test_forward_layer_matches_fp32_layer(cuda_lib, world):
 
 
 def test_wan_hook_fused_and_unfused_agree(cuda_lib):
-    """wan.self_attention_forward with plain Linear layers runs the fused
+    """wan.self_attention_forward with plain bf16 Linear layers runs the fused
     layer; with fused projections switched off it runs the module's own
     Linear layers and the pre-pass.  Both agree with the fp32 layer."""
     from powershard_b200 import wan
@@ -102,8 +102,8 @@ def test_wan_hook_fused_and_unfused_agree(cuda_lib):
     x, ws, bs, nq, nk, table = _layer_inputs(total, heads, fin, fin, 2, 11)
     module = torch.nn.Module()
     for name, w, b in zip("qkvo", ws, bs):
-        lin = torch.nn.Linear(w.shape[1], w.shape[0], device=DEV, dtype=torch.float32)
-        lin.weight.data.copy_(w.float())
+        lin = torch.nn.Linear(w.shape[1], w.shape[0], device=DEV, dtype=torch.bfloat16)
+        lin.weight.data.copy_(w)
         lin.bias.data.copy_(b)
         setattr(module, name, lin)
     module.norm_q = torch.nn.RMSNorm(heads * 128, eps=1e-6, device=DEV)
@@ -112,15 +112,16 @@ def test_wan_hook_fused_and_unfused_agree(cuda_lib):
     module.norm_k.weight.data.copy_(nk)
     module.num_heads, module.head_dim = heads, 128
     freqs = table[None, :, None]
-    xf = x.float()
+    bs = [b.bfloat16().float() for b in bs]  # the bf16 Linear layers hold bf16 biases
     outs = {}
     for fused in (True, False):
         module._ps_b200_fused_projections = fused
+        module.__dict__.pop("_ps_b200_fused_cache", None)
         module._ps_sequence = dict(total=total, enabled=False, ulysses=True, comm_dtype="bf16")
         with torch.no_grad():
-            outs[fused] = wan.self_attention_forward(module, xf, freqs)
+            outs[fused] = wan.self_attention_forward(module, x, freqs)
         module._ps_b200_engine.check()
-    assert getattr(module, "_ps_b200_fused_cache", None) is not None
+        assert (getattr(module, "_ps_b200_fused_cache", None) is not None) == fused
     for r in range(2):
         ref = layer_reference(x[r], ws, bs, nq, nk, table, heads)
         for fused in (True, False):
