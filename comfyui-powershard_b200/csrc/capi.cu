@@ -752,9 +752,8 @@ int make_map_3d(CUtensorMap* m, const void* base, bool fp16, int64_t cols, int64
   return PS_B200_OK;
 }
 
-int proj_ctas() { return sm_count(); }
-
-int64_t qkv_rows_blocks(int n) { return (int64_t(n) + 127) / 128; }
+// 128-row blocks of n GEMM rows, rounded up to whole 256-row pair tiles.
+int64_t qkv_rows_blocks(int n) { return 2 * ((int64_t(n) + 255) / 256); }
 
 }  // namespace
 }  // namespace psb
@@ -814,7 +813,7 @@ int ps_b200_qkv_proj_batch(const void* x, int64_t x_row_stride, const void* w_q,
   a.kdim = in_features;
   a.width = static_cast<int>(width);
   a.ntile_n = static_cast<int>(width / 256);
-  a.row_blocks = static_cast<int>(qkv_rows_blocks(a.n));
+  a.row_blocks = static_cast<int>(qkv_rows_blocks(a.n) / 2);
   a.epi = 1;
   a.bias[0] = b_q;
   a.bias[1] = b_k;
@@ -844,29 +843,29 @@ int ps_b200_qkv_proj_batch(const void* x, int64_t x_row_stride, const void* w_q,
     if (!workspace || workspace_bytes < need || !aligned16(workspace))
       return set_error(PS_B200_ERR_INVALID, "projection workspace of %zu bytes required", need);
     if (int rc = check_device()) return rc;
-    const int ctas = proj_ctas();
+    const bool fp16 = dtype == PS_B200_FP16;
+    const int C = proj_clusters(fp16);
+    if (C <= 0) return PS_B200_ERR_CUDA;
     const int G = a.ntile_n;
-    if (G > ctas) return set_error(PS_B200_ERR_UNSUPPORTED, "projection width above %d columns", ctas * 256);
+    if (G > C) return set_error(PS_B200_ERR_UNSUPPORTED, "projection width above %d columns", C * 256);
     a.total_groups = 2 * a.row_blocks;
-    a.groups_per_round = ctas / G;
-    a.total_tiles = a.row_blocks * G;  // v tiles
-    const int rg = (a.total_groups + a.groups_per_round - 1) / a.groups_per_round;
-    const int64_t v_in_group_rounds = int64_t(rg) * ctas - int64_t(a.total_groups) * G;
-    const int64_t v_left = a.total_tiles - v_in_group_rounds;
-    a.rounds = rg + static_cast<int>(v_left > 0 ? (v_left + ctas - 1) / ctas : 0);
+    a.total_tiles = 3 * a.row_blocks * G;  // q, k and v pair tiles, in task order
+    a.rounds = static_cast<int>((int64_t(a.total_tiles) + C - 1) / C);
+    // Statistics per 128-row block: 2 * total_groups groups (the workspace
+    // size above counts the same 2 * qkv_rows_blocks groups).
+    const int64_t groups128 = 2 * int64_t(a.total_groups);
     a.ss_part = static_cast<float*>(workspace);
-    const int64_t part_bytes = ((int64_t(a.total_groups) * G * 128 * 4 + 255) / 256) * 256;
+    const int64_t part_bytes = ((groups128 * G * 128 * 4 + 255) / 256) * 256;
     a.counters = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + part_bytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t err = cudaMemsetAsync(a.counters, 0, size_t(a.total_groups) * 4, s);
+    cudaError_t err = cudaMemsetAsync(a.counters, 0, size_t(groups128) * 4, s);
     if (err != cudaSuccess) return set_cuda_error("projection: clearing the group counters", err);
-    const bool fp16 = dtype == PS_B200_FP16;
     CUtensorMap ta, tw[3];
     if (int rc = make_map_2d(&ta, x, fp16, in_features, a.n, x_row_stride, 128)) return rc;
     const void* ws[3] = {w_q, w_k, w_v};
-    for (int i = 0; i < 3; ++i)
-      if (int rc = make_map_2d(&tw[i], ws[i], fp16, in_features, width, in_features, 256)) return rc;
-    return launch_proj(ta, tw[0], tw[1], tw[2], a, fp16, ctas, s);
+    for (int i = 0; i < 3; ++i)  // each CTA of a pair loads 128 rows of a weight tile
+      if (int rc = make_map_2d(&tw[i], ws[i], fp16, in_features, width, in_features, 128)) return rc;
+    return launch_proj(ta, tw[0], tw[1], tw[2], a, fp16, C, s);
   }
   // No local rows: only the zero padding of the send blocks.
   if (int rc = check_device()) return rc;
@@ -900,7 +899,7 @@ int ps_b200_out_proj(const void* src, int64_t src_row_stride, int64_t src_block_
   a.kdim = in_features;
   a.width = out_features;
   a.ntile_n = out_features / 256;
-  a.row_blocks = static_cast<int>(qkv_rows_blocks(n_local));
+  a.row_blocks = static_cast<int>(qkv_rows_blocks(n_local) / 2);
   a.a_mode = blocks ? 1 : 0;
   a.a_block_k = blocks ? src_block_cols : 0;
   a.epi = 0;
@@ -911,9 +910,10 @@ int ps_b200_out_proj(const void* src, int64_t src_row_stride, int64_t src_block_
   a.out_fp32 = out_dtype == PS_B200_FP32;
   a.status = status;
   a.total_tiles = a.row_blocks * a.ntile_n;
-  const int ctas = proj_ctas();
-  a.rounds = (a.total_tiles + ctas - 1) / ctas;
   const bool fp16 = dtype == PS_B200_FP16;
+  const int C = proj_clusters(fp16);
+  if (C <= 0) return PS_B200_ERR_CUDA;
+  a.rounds = (a.total_tiles + C - 1) / C;
   CUtensorMap ta, tw;
   if (blocks) {
     const int64_t nblocks = (in_features + src_block_cols - 1) / src_block_cols;
@@ -922,8 +922,8 @@ int ps_b200_out_proj(const void* src, int64_t src_row_stride, int64_t src_block_
   } else {
     if (int rc = make_map_2d(&ta, src, fp16, in_features, n_local, src_row_stride, 128)) return rc;
   }
-  if (int rc = make_map_2d(&tw, w_o, fp16, in_features, out_features, in_features, 256)) return rc;
-  return launch_proj(ta, tw, tw, tw, a, fp16, ctas, static_cast<cudaStream_t>(stream));
+  if (int rc = make_map_2d(&tw, w_o, fp16, in_features, out_features, in_features, 128)) return rc;
+  return launch_proj(ta, tw, tw, tw, a, fp16, C, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -107,7 +107,7 @@ struct ProjArgs {
   int kdim;                // K: input features (a multiple of 64)
   int width;               // output features of one projection (a multiple of 256)
   int ntile_n;             // width / 256: column tiles of one projection
-  int row_blocks;          // ceil(n / 128)
+  int row_blocks;          // ceil(n / 256): row blocks of the 256-row pair tiles
   int a_mode;              // 0: A is [n][kdim] rows; 1: A is [src][n][a_block_k] blocks (k = src*a_block_k + c)
   int a_block_k;           // columns per source block (a multiple of 64) for a_mode 1
   int epi;                 // 0: y = A W^T + b stored row-major; 1: q/k/v with RMSNorm, RoPE and the Ulysses pack
@@ -123,19 +123,23 @@ struct ProjArgs {
   void* out;               // epi 0: [n][width] (row stride out_row_stride elements)
   int64_t out_row_stride;
   int out_fp32;
-  // Scheduling (persistent CTAs, one task = one 128 x 256 tile per round):
-  int groups_per_round;    // epi 1: whole q/k groups (ntile_n tiles of one row block) per round
-  int total_groups;        // epi 1: 2 * row_blocks
-  int total_tiles;         // epi 0: row_blocks * ntile_n; epi 1: v tiles, row_blocks * ntile_n
+  // Scheduling (persistent CTA pairs, one task = one 256 x 256 pair tile per round):
+  int groups_per_round;    // unused (kept for the layout of this struct)
+  int total_groups;        // epi 1: 2 * row_blocks q/k groups of pair tiles
+  int total_tiles;         // epi 0: row_blocks * ntile_n; epi 1: 3 * row_blocks * ntile_n
   int rounds;
-  float* ss_part;          // epi 1: [total_groups][ntile_n][128] partial sums of squares
-  unsigned* counters;      // epi 1: [total_groups] tiles of the group that posted their partials (zeroed)
+  // RMSNorm statistics per 128-row block (two per pair row block):
+  float* ss_part;          // epi 1: [4 * row_blocks][ntile_n][128] partial sums of squares
+  unsigned* counters;      // epi 1: [4 * row_blocks] tiles that posted their partials (zeroed)
   int* status;             // device status word, may be null
 };
 
-// Launches the projection GEMM (cooperative: every CTA resident, one per SM).
+// Launches the projection GEMM: `clusters` pairs of CTAs (cooperative
+// cluster launch: every CTA resident, one per SM).
 int launch_proj(const CUtensorMap& ta, const CUtensorMap& tw0, const CUtensorMap& tw1, const CUtensorMap& tw2,
-                const ProjArgs& args, bool fp16, int ctas, cudaStream_t stream);
+                const ProjArgs& args, bool fp16, int clusters, cudaStream_t stream);
+// CTA pairs the device keeps resident at once (0 on error, recorded).
+int proj_clusters(bool fp16);
 
 struct BroadcastArgs {
   const void* src;         // 16-byte vectors to copy

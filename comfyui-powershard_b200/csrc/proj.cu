@@ -11,20 +11,33 @@
 //     staging rows, or the NCCL receive buffer's per-source blocks (a_mode 1)
 //     - so no unpack pass runs before the GEMM.
 //
-// The row statistic of RMSNorm spans all width/256 column tiles of a row
-// block, which run on different CTAs.  The kernel is persistent (one CTA per
-// SM, cooperative launch: every CTA resident) and works in rounds; a round
-// holds whole q/k groups (the width/256 tiles of one row block's q or k),
-// so all tiles of a group are in flight at once.  Each posts its per-row
-// partial sum of squares and bumps the group's counter; once the counter
-// reaches the group size, every tile adds the partials in a fixed order (the
-// same bits on every tile and every run) and normalises.  v tiles and, with
-// epi 0, all tiles have no such dependence and fill the remaining slots.
+// Two-SM tiles: a cluster of two CTAs computes one 256 x 256 output tile
+// with tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  CTA r of the pair
+// loads rows [128 r, 128 r + 128) of the tile's A and rows [128 r, 128 r +
+// 128) of its B (weight) tile into its own shared memory, and holds its 128
+// rows of the fp32 accumulator in its own TMEM.  Each SM thus streams half
+// of B instead of all of it: per 64-wide k-block 64 KB of shared-memory
+// traffic (TMA writes + UMMA reads) against 96 KB for a one-SM 128 x 256
+// tile, which is what keeps the tensor pipe fed at ~128 bytes per clock.
+// The even CTA issues every UMMA and commits to both CTAs' barriers; both
+// CTAs' loads of a stage complete on the even CTA's full barrier.  No load
+// uses multicast.
 //
-// Warp roles (192 threads): warps 0-3 epilogue (thread = one row of the
-// tile, TMEM lane), warp 4 TMA producer (4-stage ring of 128x64 A and
-// 256x64 B tiles, 128-byte swizzle), warp 5 TMEM allocation + UMMA issuer
-// (M=128 N=256 K=16, fp32 accumulators, two 256-column TMEM buffers so the
+// The row statistic of RMSNorm spans all width/256 column tiles of a 128-row
+// block, which run on different clusters.  The kernel is persistent (one
+// CTA per SM, cooperative cluster launch: every CTA resident) and runs its
+// tasks in rounds of one pair tile per cluster, in a linear order (task_of)
+// that keeps one projection's weight hot in L2 at a time.  Each CTA posts its
+// rows' partial sums of squares and bumps the counter of its 128-row block;
+// once the counter reaches the group size (the width/256 tiles of that
+// block's q or k), every tile adds the partials in a fixed order (the same
+// bits on every tile and every run) and normalises.  v tiles and, with
+// epi 0, all tiles have no such dependence.
+//
+// Warp roles (192 threads per CTA): warps 0-3 epilogue (thread = one row of
+// the CTA's half tile, TMEM lane), warp 4 TMA producer (6-stage ring of
+// 128x64 A and 128x64 B halves, 128-byte swizzle), warp 5 TMEM allocation
+// and, in the even CTA, the UMMA issuer (two 256-column TMEM buffers so the
 // epilogue of one tile overlaps the main loop of the next).  Every wait,
 // including the wait for a group's partials, is bounded.
 #include "ptx.cuh"
@@ -37,12 +50,12 @@
 namespace psb {
 namespace proj {
 
-constexpr int kBM = 128;
-constexpr int kBN = 256;
+constexpr int kBM = 128;               // rows per CTA (256 per pair tile)
+constexpr int kBN = 256;               // columns per pair tile (128 of B per CTA)
 constexpr int kBK = 64;
-constexpr int kStages = 4;
-constexpr int kAStage = kBM * kBK * 2;  // 16 KiB
-constexpr int kBStage = kBN * kBK * 2;  // 32 KiB
+constexpr int kStages = 6;
+constexpr int kAStage = kBM * kBK * 2;        // 16 KiB
+constexpr int kBStage = (kBN / 2) * kBK * 2;  // 16 KiB: this CTA's half of B
 constexpr int kThreads = 192;
 constexpr int kSmemBarOff = kStages * (kAStage + kBStage);
 enum Bar : int {
@@ -82,54 +95,37 @@ __device__ __forceinline__ uint16_t from_f(float f) {
   }
 }
 
-// One task: a 128 x 256 output tile of one projection.
+// One task: a 256 x 256 output tile of one projection (one CTA pair).
 struct Task {
   bool valid;
   int kind;   // 0 q, 1 k, 2 v (epi 1); 0 (epi 0)
-  int rb;     // row block
+  int rb;     // 256-row block
   int tile;   // column tile within the projection
   int group;  // epi 1, q/k: rb * 2 + kind
 };
 
-// Task of CTA c in round r (P CTAs).  epi 1: round r < rg holds whole q/k
-// groups in its first ng * G slots and v tiles after them; later rounds
-// hold only v tiles.  epi 0: tiles in order.
+// Task of cluster c in round r (P clusters): task index r * P + c in one
+// linear order - epi 1: every q tile, then every k tile, then every v tile,
+// each kind row block by row block (so one kind's weight stays in L2 while
+// its tiles run); epi 0: row block by row block.  A q/k group is the ntile_n
+// consecutive tiles of one row block and may straddle two rounds.  No wait
+// cycle can form: a tile's epilogue waits only for its group, whose tiles sit
+// on ntile_n distinct clusters (the host requires P >= ntile_n), and every
+// cluster runs its tasks in increasing index order, so by induction on the
+// group index every group completes.
 __device__ __forceinline__ Task task_of(const ProjArgs& a, int r, int c, int P) {
   Task t{false, 0, 0, 0, 0};
   const int G = a.ntile_n;
-  if (a.epi == 0) {
-    const int idx = r * P + c;
-    if (idx < a.total_tiles) {
-      t.valid = true;
-      t.rb = idx / G;
-      t.tile = idx - t.rb * G;
-    }
-    return t;
-  }
-  const int gpr = a.groups_per_round;
-  const int rg = (a.total_groups + gpr - 1) / gpr;
-  int vidx;
-  if (r < rg) {
-    const int g0 = r * gpr;
-    const int ng = min(gpr, a.total_groups - g0);
-    if (c < ng * G) {
-      t.valid = true;
-      t.group = g0 + c / G;
-      t.tile = c - (c / G) * G;
-      t.kind = t.group & 1;
-      t.rb = t.group >> 1;
-      return t;
-    }
-    vidx = r * P - g0 * G + (c - ng * G);
-  } else {
-    vidx = rg * P - a.total_groups * G + (r - rg) * P + c;
-  }
-  if (vidx < a.total_tiles) {
-    t.valid = true;
-    t.kind = 2;
-    t.rb = vidx / G;
-    t.tile = vidx - t.rb * G;
-  }
+  const int64_t idx = static_cast<int64_t>(r) * P + c;
+  if (idx >= a.total_tiles) return t;
+  const int64_t per_kind = static_cast<int64_t>(a.row_blocks) * G;
+  const int kind = a.epi == 1 ? static_cast<int>(idx / per_kind) : 0;
+  const int j = static_cast<int>(idx - kind * per_kind);
+  t.valid = true;
+  t.kind = kind;
+  t.rb = j / G;
+  t.tile = j - t.rb * G;
+  t.group = t.rb * 2 + kind;
   return t;
 }
 
@@ -220,31 +216,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int P = gridDim.x;
-  const int c = blockIdx.x;
+  const int P = gridDim.x >> 1;  // clusters
+  const int c = blockIdx.x >> 1;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   const int ksteps = a.kdim / kBK;
   int* status = a.status;
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  // The even CTA's barrier i, and barrier i of CTA r, as shared::cluster addresses.
+  auto lead_bar = [&](int i) { return mapa_shared(bar(i), 0); };
+  auto cta_bar = [&](int i, uint32_t r) { return mapa_shared(bar(i), r); };
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kFull + s), 1);
-      mbar_init(bar(kEmpty + s), 1);
+      mbar_init(bar(kFull + s), 1);   // even CTA: its producer's arrive + both CTAs' bytes
+      mbar_init(bar(kEmpty + s), 1);  // the issuer's commit, in each CTA
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(kAccFull + b), 1);
-      mbar_init(bar(kAccEmpty + b), 4);
+      mbar_init(bar(kAccFull + b), 1);   // the issuer's commit, in each CTA
+      mbar_init(bar(kAccEmpty + b), 8);  // even CTA: the 4 epilogue warps of each CTA
     }
     mbar_init(bar(kDrain), 1);
     fence_mbar_init();
   }
   if (warp == 5) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -259,31 +260,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Task t = task_of(a, r, c, P);
         if (!t.valid) continue;
         const CUtensorMap* mw = t.kind == 0 ? &tm_w0 : (t.kind == 1 ? &tm_w1 : &tm_w2);
-        const int row0 = t.rb * kBM, n0 = t.tile * kBN;
+        const int row0 = (t.rb * 2 + static_cast<int>(rank)) * kBM;
+        const int n0 = t.tile * kBN + static_cast<int>(rank) * (kBN / 2);
         for (int kk = 0; kk < ksteps; ++kk, ++it) {
           const int s = it % kStages;
           if (it >= kStages) {
             ok = mbar_wait(bar(kEmpty + s), ((it / kStages) - 1) & 1u, abort_flag, status, kErrEmpty);
             if (!ok) break;
           }
-          mbar_arrive_expect_tx(bar(kFull + s), kAStage + kBStage);
+          // The even CTA's full barrier counts both CTAs' halves of the stage.
+          if (leader) mbar_arrive_expect_tx(bar(kFull + s), 2 * (kAStage + kBStage));
+          const uint32_t fb = lead_bar(kFull + s);
           const int k0 = kk * kBK;
           if (a.a_mode == 0) {
-            tma_load_2d(smem_u32(sA + s * kAStage), &tm_a, bar(kFull + s), k0, row0);
+            tma_load_2d_pair(smem_u32(sA + s * kAStage), &tm_a, fb, k0, row0);
           } else {
             const int src = k0 / a.a_block_k;
-            tma_load_3d(smem_u32(sA + s * kAStage), &tm_a, bar(kFull + s), k0 - src * a.a_block_k, row0, src);
+            tma_load_3d_pair(smem_u32(sA + s * kAStage), &tm_a, fb, k0 - src * a.a_block_k, row0, src);
           }
-          tma_load_2d(smem_u32(sB + s * kBStage), mw, bar(kFull + s), k0, n0);
+          tma_load_2d_pair(smem_u32(sB + s * kBStage), mw, fb, k0, n0);
         }
       }
-      // Every copy issued lands before the CTA may exit.
-      for (int j = max(0, it - kStages); j < it; ++j) drain_wait(bar(kFull + j % kStages), (j / kStages) & 1u, status);
+      // Every copy issued lands before the pair may exit: the even CTA's full
+      // barriers count both CTAs' copies (the odd CTA waits at the final
+      // cluster barrier until the even CTA has drained them).
+      if (leader)
+        for (int j = max(0, it - kStages); j < it; ++j)
+          drain_wait(bar(kFull + j % kStages), (j / kStages) & 1u, status);
     }
   } else if (warp == 5) {
-    // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16(kBM, kBN, !kFp16, false, false);
+    // ------------------------------------------------------------ UMMA issuer (even CTA)
+    if (lane == 0 && leader) {
+      const uint32_t idesc = idesc_f16(2 * kBM, kBN, !kFp16, false, false);
       const uint64_t da = sdesc_sw128(smem_u32(sA), 16, 1024);
       const uint64_t db = sdesc_sw128(smem_u32(sB), 16, 1024);
       int it = 0, seq = 0;
@@ -307,14 +315,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t dbs = db + static_cast<uint64_t>((s * kBStage) >> 4);
 #pragma unroll
           for (int j = 0; j < kBK / 16; ++j)
-            umma_ss(acc, das + ((32 * j) >> 4), dbs + ((32 * j) >> 4), idesc, (kk | j) != 0 ? 1u : 0u);
-          umma_commit(bar(kEmpty + s));
+            umma_ss_pair(acc, das + ((32 * j) >> 4), dbs + ((32 * j) >> 4), idesc, (kk | j) != 0 ? 1u : 0u);
+          umma_commit_pair(cta_bar(kEmpty + s, 0));
+          umma_commit_pair(cta_bar(kEmpty + s, 1));
         }
         if (!ok) break;
-        umma_commit(bar(kAccFull + b));
+        umma_commit_pair(cta_bar(kAccFull + b, 0));
+        umma_commit_pair(cta_bar(kAccFull + b, 1));
         ++seq;
       }
-      umma_commit(bar(kDrain));
+      umma_commit_pair(cta_bar(kDrain, 0));
       drain_wait(bar(kDrain), 0, status);
     }
   } else {
@@ -333,7 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = warp_wait(bar(kAccFull + b), ((seq - 1) >> 1) & 1u, abort_flag, status, kErrAcc);
       tc_fence_after();
       const uint32_t acc = tmem + lane_off + b * kBN;
-      const int m = t.rb * kBM + row;  // GEMM row
+      const int rb128 = t.rb * 2 + static_cast<int>(rank);  // this CTA's 128-row block
+      const int m = rb128 * kBM + row;                      // GEMM row
       const bool live = m < a.n;
       // epi 1: batch row and token of GEMM row m; epi 0: the token itself.
       const int bi = a.epi == 1 ? m / a.n_local : 0;
@@ -385,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          float* part = a.ss_part + static_cast<int64_t>(t.group) * G * kBM;
+          const int group = rb128 * 2 + t.kind;  // the 128-row block's q or k group
+          float* part = a.ss_part + static_cast<int64_t>(group) * G * kBM;
           part[t.tile * kBM + row] = ss;
           __threadfence();  // every writer's partial is visible GPU-wide before the group counter moves
           named_bar_sync(1, 128);
@@ -394,10 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           // partials of its row in tile order.
           if (threadIdx.x == 0) {
             __threadfence();
-            red_release_gpu_add(a.counters + t.group, 1u);
+            red_release_gpu_add(a.counters + group, 1u);
             const uint64_t t0 = globaltimer();
             bool waited = true;
-            while (ld_acquire_gpu(a.counters + t.group) < static_cast<unsigned>(G)) {
+            while (ld_acquire_gpu(a.counters + group) < static_cast<unsigned>(G)) {
               if (*abort_flag || globaltimer() - t0 > kWaitLimitNs) {
                 waited = false;
                 break;
@@ -463,15 +475,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(kAccEmpty + b));
+      if (lane == 0) mbar_arrive_cluster(lead_bar(kAccEmpty + b));
     }
   }
 
+  // Both CTAs' UMMAs, copies and TMEM reads are complete before either CTA
+  // frees TMEM or exits (the even CTA's UMMAs read the odd CTA's shared
+  // memory and write its TMEM).
   tc_fence_before();
   __syncthreads();
+  cluster_sync();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -523,10 +539,51 @@ int prepare_proj() {
   done[dev] = true;
   return 0;
 }
+
+template <bool kFp16>
+cudaLaunchConfig_t proj_config(int clusters, cudaStream_t stream, cudaLaunchAttribute (&attrs)[2]) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(proj::kThreads);
+  cfg.dynamicSmemBytes = proj::kSmemBytes;
+  cfg.stream = stream;
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeCooperative;
+  attrs[1].val.cooperative = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  return cfg;
+}
 }  // namespace
 
+// CTA pairs the device keeps resident at once (the persistent grid), queried
+// once per device and dtype; 0 on error (with the error recorded).
+int proj_clusters(bool fp16) {
+  static int cached[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  int& slot = cached[dev][fp16 ? 1 : 0];
+  if (slot > 0) return slot;
+  if ((fp16 ? prepare_proj<true>() : prepare_proj<false>()) != 0) return 0;
+  cudaLaunchAttribute attrs[2];
+  cudaLaunchConfig_t cfg = fp16 ? proj_config<true>(1, nullptr, attrs) : proj_config<false>(1, nullptr, attrs);
+  cfg.numAttrs = 1;  // the occupancy query takes the cluster shape only
+  int n = 0;
+  const cudaError_t err = fp16 ? cudaOccupancyMaxActiveClusters(&n, proj::proj_kernel<true>, &cfg)
+                               : cudaOccupancyMaxActiveClusters(&n, proj::proj_kernel<false>, &cfg);
+  if (err != cudaSuccess || n <= 0) {
+    set_cuda_error("projection: cudaOccupancyMaxActiveClusters", err != cudaSuccess ? err : cudaErrorInvalidValue);
+    return 0;
+  }
+  slot = n;
+  return n;
+}
+
 int launch_proj(const CUtensorMap& ta, const CUtensorMap& tw0, const CUtensorMap& tw1, const CUtensorMap& tw2,
-                const ProjArgs& args, bool fp16, int ctas, cudaStream_t stream) {
+                const ProjArgs& args, bool fp16, int clusters, cudaStream_t stream) {
   using namespace proj;
   if (args.epi == 1) {
     const int64_t pads = (static_cast<int64_t>(args.seg_rows - args.n_local) * args.world * args.heads_per_rank +
@@ -541,17 +598,16 @@ int launch_proj(const CUtensorMap& ta, const CUtensorMap& tw0, const CUtensorMap
     }
   }
   if (args.rounds <= 0) return 0;
-  void* params[] = {const_cast<CUtensorMap*>(&ta), const_cast<CUtensorMap*>(&tw0), const_cast<CUtensorMap*>(&tw1),
-                    const_cast<CUtensorMap*>(&tw2), const_cast<ProjArgs*>(&args)};
+  cudaLaunchAttribute attrs[2];
   cudaError_t err;
   if (fp16) {
     if (int rc = prepare_proj<true>()) return rc;
-    err = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(proj_kernel<true>), dim3(ctas), dim3(kThreads),
-                                      params, kSmemBytes, stream);
+    const cudaLaunchConfig_t cfg = proj_config<true>(clusters, stream, attrs);
+    err = cudaLaunchKernelEx(&cfg, proj_kernel<true>, ta, tw0, tw1, tw2, args);
   } else {
     if (int rc = prepare_proj<false>()) return rc;
-    err = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(proj_kernel<false>), dim3(ctas), dim3(kThreads),
-                                      params, kSmemBytes, stream);
+    const cudaLaunchConfig_t cfg = proj_config<false>(clusters, stream, attrs);
+    err = cudaLaunchKernelEx(&cfg, proj_kernel<false>, ta, tw0, tw1, tw2, args);
   }
   if (err != cudaSuccess) return set_cuda_error("projection launch", err);
   count_launch();
