@@ -53,7 +53,10 @@ namespace proj {
 constexpr int kBM = 128;               // rows per CTA (256 per pair tile)
 constexpr int kBN = 256;               // columns per pair tile (128 of B per CTA)
 constexpr int kBK = 64;
-constexpr int kStages = 6;
+#ifndef PSB_PROJ_STAGES
+#define PSB_PROJ_STAGES 6
+#endif
+constexpr int kStages = PSB_PROJ_STAGES;  // 32 KiB each
 constexpr int kAStage = kBM * kBK * 2;        // 16 KiB
 constexpr int kBStage = (kBN / 2) * kBK * 2;  // 16 KiB: this CTA's half of B
 constexpr int kThreads = 192;
