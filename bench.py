@@ -102,8 +102,8 @@ def peaks():
     return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s"
 
 
-TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one attention launch at L=8192 "
-                  "(profiles/ncu_traffic.txt), scaled by tokens and by heads per rank; not measured at full size")
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one full-size attention launch at W=1 "
+                  "(profiles/ncu_traffic.txt); for W > 1 scaled by heads per rank, not measured there")
 
 
 def traffic_per_launch(world):
