@@ -682,7 +682,15 @@ def main():
                      "CUDA events, max over ranks")
     comm = measure_comm(engine, proj, norm_w, freqs, geo, dev, ms, attn_ms) if world > 1 else None
     del proj
-    layer = None if args.no_layer else measure_layer(engine, geo, freqs, dev, world)
+    layer = None
+    if not args.no_layer:
+        # Outside the timed region and not part of the metric: a failure here
+        # (argument checks fail alike on every rank, before any collective) is
+        # reported in the line instead of ending the run.
+        try:
+            layer = measure_layer(engine, geo, freqs, dev, world)
+        except (RuntimeError, ValueError) as exc:
+            layer = dict(error=f"{type(exc).__name__}: {str(exc)[:300]}")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
