@@ -31,24 +31,26 @@ def _ref_matmul(a, w, b):
     return y if b is None else y + b.float()
 
 
-@pytest.mark.parametrize("n,fin,fout", [(1, 64, 256), (300, 512, 512), (1000, 1536, 1536), (4095, 5120, 5120)])
-def test_out_projection_rows(cuda_lib, n, fin, fout):
-    """fp32 output against torch's fp32 matmul; the bf16 output is exactly the
-    fp32 output rounded once (same accumulation, one rounding)."""
+@pytest.mark.parametrize("n,fin,fout,dtype", [(1, 64, 256, torch.bfloat16), (300, 512, 512, torch.bfloat16),
+                                              (1000, 1536, 1536, torch.bfloat16), (4095, 5120, 5120, torch.bfloat16),
+                                              (700, 768, 512, torch.float16), (257, 512, 256, torch.float16)])
+def test_out_projection_rows(cuda_lib, n, fin, fout, dtype):
+    """fp32 output against torch's fp32 matmul; the 16-bit output is exactly
+    the fp32 output rounded once (same accumulation, one rounding)."""
     from powershard_b200 import ops
     g = torch.Generator(device=DEV).manual_seed(n + fin)
-    a = torch.randn(n, fin, device=DEV, generator=g).bfloat16()
-    w = (torch.randn(fout, fin, device=DEV, generator=g) * 0.02).bfloat16()
+    a = torch.randn(n, fin, device=DEV, generator=g).to(dtype)
+    w = (torch.randn(fout, fin, device=DEV, generator=g) * 0.02).to(dtype)
     b = torch.randn(fout, device=DEV, generator=g) * 0.1
     out32 = torch.empty(n, fout, device=DEV, dtype=torch.float32)
-    out16 = torch.empty(n, fout, device=DEV, dtype=torch.bfloat16)
+    out16 = torch.empty(n, fout, device=DEV, dtype=dtype)
     status = ops.DeviceStatus(DEV)
     ops.out_projection(a, w, b, out32, n, fin, a.stride(0), status=status)
     ops.out_projection(a, w, b, out16, n, fin, a.stride(0), status=status)
     status.check()
     ref = _ref_matmul(a, w, b)
     assert float((out32 - ref).abs().max()) <= 1e-3 * max(1.0, float(ref.abs().max()))
-    assert torch.equal(out16, out32.bfloat16())
+    assert torch.equal(out16, out32.to(dtype))
 
 
 def test_out_projection_from_exchange_buffers(cuda_lib):
@@ -82,33 +84,38 @@ def test_out_projection_from_exchange_buffers(cuda_lib):
 
 
 def _qkv_reference(x, ws, bs, nq, nk, table, heads, eps=1e-6):
-    """attention_qkv on the fp32 projections: RMSNorm rounded to bf16, RoPE in
-    fp32, cast to the bf16 wire; v is the projection rounded once."""
+    """attention_qkv on the fp32 projections: RMSNorm rounded to the wire
+    type, RoPE in fp32, cast to the wire; v is the projection rounded once."""
+    wire = x.dtype
     outs = []
     for i, (w, b) in enumerate(zip(ws, bs)):
         y = _ref_matmul(x, w, b)
         if i < 2:
             nw = (nq, nk)[i].float()
-            y = (y * torch.rsqrt(y.square().mean(-1, keepdim=True) + eps) * nw).bfloat16().float()
+            y = (y * torch.rsqrt(y.square().mean(-1, keepdim=True) + eps) * nw).to(wire).float()
             y = y.view(y.shape[0], heads, -1, 1, 2)
             rot = table[:, None]
             y = (rot[..., 0] * y[..., 0] + rot[..., 1] * y[..., 1]).reshape(y.shape[0], heads, -1)
         else:
             y = y.view(y.shape[0], heads, -1)
-        outs.append(y.bfloat16())
+        outs.append(y.to(wire))
     return outs
 
 
-@pytest.mark.parametrize("total,heads,world,fin", [(300, 4, 1, 512), (1000, 12, 2, 1536), (41, 6, 4, 256),
-                                                   (4095, 40, 1, 5120), (1500, 40, 8, 5120)])
-def test_qkv_projection_matches_attention_qkv(cuda_lib, total, heads, world, fin):
+@pytest.mark.parametrize("total,heads,world,fin,dtype", [(300, 4, 1, 512, torch.bfloat16),
+                                                         (1000, 12, 2, 1536, torch.bfloat16),
+                                                         (41, 6, 4, 256, torch.bfloat16),
+                                                         (4095, 40, 1, 5120, torch.bfloat16),
+                                                         (1500, 40, 8, 5120, torch.bfloat16),
+                                                         (700, 8, 2, 1024, torch.float16)])
+def test_qkv_projection_matches_attention_qkv(cuda_lib, total, heads, world, fin, dtype):
     from powershard_b200 import ops
     from powershard_b200.partition import UlyssesGeometry
     from powershard_b200.rope import rope_table_3d
     d = 128
     g = torch.Generator(device=DEV).manual_seed(total + heads)
-    x_all = torch.randn(total, fin, device=DEV, generator=g).bfloat16()
-    ws = [(torch.randn(heads * d, fin, device=DEV, generator=g) * 0.02).bfloat16() for _ in range(3)]
+    x_all = torch.randn(total, fin, device=DEV, generator=g).to(dtype)
+    ws = [(torch.randn(heads * d, fin, device=DEV, generator=g) * 0.02).to(dtype) for _ in range(3)]
     bs = [torch.randn(heads * d, device=DEV, generator=g) * 0.05 for _ in range(3)]
     nq = torch.rand(heads * d, device=DEV, generator=g) + 0.5
     nk = torch.rand(heads * d, device=DEV, generator=g) + 0.5
@@ -119,7 +126,7 @@ def test_qkv_projection_matches_attention_qkv(cuda_lib, total, heads, world, fin
     for rank in range(world):
         geo = UlyssesGeometry(total=total, heads=heads, head_dim=d, world=world, rank=rank)
         a, b = geo.bounds
-        send = torch.full(geo.send_shape(), float("nan"), device=DEV, dtype=torch.bfloat16)
+        send = torch.full(geo.send_shape(), float("nan"), device=DEV, dtype=dtype)
         wsp = ops.projection_workspace(geo.n_local, heads, d, DEV)
         ops.qkv_projection(x_all[a:b], *ws, *bs, nq, nk, table[a:b], ops.send_blocks(send), geo, 1e-6, wsp,
                            status)
@@ -128,7 +135,7 @@ def test_qkv_projection_matches_attention_qkv(cuda_lib, total, heads, world, fin
         h = geo.heads_per_rank
         flat = send.permute(1, 2, 0, 3, 4).reshape(3, geo.width, world * h, d)
         assert not flat[:, b - a:].any() and not flat[:, :, heads:].any()
-        ulp = 2.0 ** -7
+        ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
         for kind in range(3):
             got = flat[kind, :b - a, :heads].float()
             want = refs[kind][a:b].float()
