@@ -124,7 +124,6 @@ struct ProjArgs {
   int64_t out_row_stride;
   int out_fp32;
   // Scheduling (persistent CTA pairs, one task = one 256 x 256 pair tile per round):
-  int groups_per_round;    // unused (kept for the layout of this struct)
   int total_groups;        // epi 1: 2 * row_blocks q/k groups of pair tiles
   int total_tiles;         // epi 0: row_blocks * ntile_n; epi 1: 3 * row_blocks * ntile_n
   int rounds;
