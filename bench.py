@@ -417,7 +417,7 @@ def measure_comm(engine, proj, norm_w, freqs, geo, dev, ms_step, attn_ms):
     return res
 
 
-def measure_layer(engine, geo, freqs, dev, world, reps=5):
+def measure_layer(engine, geo, freqs, dev, world, reps=3, rounds=3):
     """The whole self-attention layer (powershard/wan_model.py:421-438) of the
     configs[1] shape, outside the headline timing: x [1, n, 5120] bf16 and
     random bf16 q/k/v/o weights.  fused = UlyssesAttention.forward_layer (the
@@ -459,21 +459,28 @@ def measure_layer(engine, geo, freqs, dev, world, reps=5):
             events[name].append((s, e))
         return run
 
+    # The two paths alternate (same clocks and power state for both: the SM
+    # clock drifts under the power cap); each figure is the median of its
+    # rounds.
+    samples = {"cublas": [], "fused": [], "gemm_qkv": [], "gemm_o": []}
+    for rnd in range(rounds):
+        sync_all()
+        samples["cublas"].append(time_events(cublas, reps, warm=2 if rnd == 0 else 1))
+        samples["gemm_qkv"].append(time_events(lambda: [x[0] @ w.t() for w in ws[:3]], reps, warm=1))
+        samples["gemm_o"].append(time_events(lambda: x[0] @ ws[3].t(), reps, warm=1))
+        sync_all()
+        for name in events:
+            setattr(ops, name, timed(name))
+        try:
+            samples["fused"].append(time_events(fused, reps, warm=2 if rnd == 0 else 1))
+        finally:
+            for name, fn in orig.items():
+                setattr(ops, name, fn)
+    t_cublas, t_fused = statistics.median(samples["cublas"]), statistics.median(samples["fused"])
+    t_gemm_qkv, t_gemm_o = statistics.median(samples["gemm_qkv"]), statistics.median(samples["gemm_o"])
     sync_all()
-    t_cublas = time_events(cublas, reps)
-    sync_all()
-    for name in events:
-        setattr(ops, name, timed(name))
-    try:
-        t_fused = time_events(fused, reps)
-    finally:
-        for name, fn in orig.items():
-            setattr(ops, name, fn)
-    sync_all()
-    t_gemm_qkv = time_events(lambda: [x[0] @ w.t() for w in ws[:3]], reps)
-    t_gemm_o = time_events(lambda: x[0] @ ws[3].t(), reps)
     engine.check()
-    per = {k: statistics.mean(s.elapsed_time(e) for s, e in v[2:]) for k, v in events.items()}
+    per = {k: statistics.median(s.elapsed_time(e) for s, e in v) for k, v in events.items()}
     vals = torch.tensor([t_fused, t_cublas, per["qkv_projection"], per["out_projection"], t_gemm_qkv, t_gemm_o],
                         device=dev, dtype=torch.float64)
     if world > 1:
@@ -491,6 +498,7 @@ def measure_layer(engine, geo, freqs, dev, world, reps=5):
         qkv_cublas_ms=t_gemm_qkv, qkv_cublas_tflops=tf(6.0 * n * HIDDEN * HIDDEN, t_gemm_qkv),
         out_gemm_ms=t_o, out_gemm_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_o),
         out_cublas_ms=t_gemm_o, out_cublas_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_gemm_o),
+        rounds=rounds, reps_per_round=reps,
         what="whole layer, x [1, n_local, 5120] bf16 -> [1, n_local, 5120]: fused = forward_layer (qkv GEMM with "
              "RMSNorm/RoPE/pack epilogue, exchange, attention, o GEMM from the exchange buffer); cublas = torch "
              "matmuls + engine.forward (pre-pass, exchange, attention, unpack); *_gemm = the fused GEMM kernels "
