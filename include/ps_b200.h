@@ -350,7 +350,9 @@ int ps_b200_unpack_batch(const void* recv, int64_t src_stride, int64_t batch_str
                          int n_local, int heads, int heads_per_rank, int head_dim, void* stream);
 
 /*
- * Projection GEMMs (tcgen05, one persistent CTA per SM, cooperative launch).
+ * Projection GEMMs (tcgen05.mma.cta_group::2 on 256x256 tiles, one persistent
+ * pair of CTAs per two SMs, cooperative cluster launch: the grid is every pair
+ * the device keeps resident, so nothing else should hold SMs the call needs).
  *
  * ps_b200_qkv_proj: q|k|v = x [W_q|W_k|W_v]^T + b for this rank's n_local
  *   tokens, x [n_local][in_features] (row stride x_row_stride), weights
