@@ -486,6 +486,7 @@ def measure_layer(engine, geo, freqs, dev, world, reps=3, rounds=3):
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     t_fused, t_cublas, t_qkv, t_o, t_gemm_qkv, t_gemm_o = vals.tolist()
+    e2e_wan = measure_e2e_wan(x, ws, norm, freqs, geo, dev, world, reps)
     attn_flops = 4.0 * total * total * HEADS * DIM
     proj_flops = 2.0 * total * HIDDEN * HIDDEN * 4          # the whole layer's four projections
     del x, ws
@@ -498,11 +499,61 @@ def measure_layer(engine, geo, freqs, dev, world, reps=3, rounds=3):
         qkv_cublas_ms=t_gemm_qkv, qkv_cublas_tflops=tf(6.0 * n * HIDDEN * HIDDEN, t_gemm_qkv),
         out_gemm_ms=t_o, out_gemm_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_o),
         out_cublas_ms=t_gemm_o, out_cublas_tflops=tf(2.0 * n * HIDDEN * HIDDEN, t_gemm_o),
-        rounds=rounds, reps_per_round=reps,
+        rounds=rounds, reps_per_round=reps, e2e_wan=e2e_wan,
         what="whole layer, x [1, n_local, 5120] bf16 -> [1, n_local, 5120]: fused = forward_layer (qkv GEMM with "
              "RMSNorm/RoPE/pack epilogue, exchange, attention, o GEMM from the exchange buffer); cublas = torch "
              "matmuls + engine.forward (pre-pass, exchange, attention, unpack); *_gemm = the fused GEMM kernels "
              "alone (events around each launch), *_cublas = torch matmuls of the same shapes (q/k/v: three)")
+
+
+def measure_e2e_wan(x, ws, norm, freqs, geo, dev, world, reps):
+    """The layer end to end through the entry a PowerShard worker installs:
+    wan.self_attention_forward on a module with bf16 q/k/v/o Linear layers
+    and RMSNorm q/k (the shape install_wan_compute routes), x copied from
+    pinned host memory and the output copied back every step, in order on
+    one stream.  Max over ranks."""
+    from powershard_b200 import wan
+    n = geo.n_local
+    module = torch.nn.Module()
+    for name, w in zip("qkvo", ws):
+        lin = torch.nn.Linear(HIDDEN, HIDDEN, bias=False, device=dev, dtype=torch.bfloat16)
+        lin.weight.data.copy_(w)
+        setattr(module, name, lin)
+    module.norm_q = torch.nn.RMSNorm(HIDDEN, eps=1e-6, device=dev)
+    module.norm_k = torch.nn.RMSNorm(HIDDEN, eps=1e-6, device=dev)
+    module.norm_q.weight.data.copy_(norm)
+    module.norm_k.weight.data.copy_(norm)
+    module.num_heads, module.head_dim = HEADS, DIM
+    module._ps_sequence = dict(total=geo.total, enabled=world > 1, ulysses=True, comm_dtype="bf16")
+    table = freqs[None, :, None]
+    host_x = x.cpu().pin_memory()
+    host_out = torch.empty_like(host_x).pin_memory()
+    dev_x = torch.empty_like(x)
+
+    def step():
+        dev_x.copy_(host_x, non_blocking=True)
+        with torch.no_grad():
+            out = wan.self_attention_forward(module, dev_x, table)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    ms = time_events(step, reps, warm=0)
+    module._ps_b200_engine.check()
+    fused = getattr(module, "_ps_b200_fused_cache", None) is not None
+    val = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(val, op=dist.ReduceOp.MAX)
+        module._ps_b200_engine.close()
+    ms = float(val[0])
+    nbytes = n * HIDDEN * 2
+    return dict(ms_per_layer=ms, fused_layer=fused, h2d_bytes_per_step=nbytes, d2h_bytes_per_step=nbytes,
+                attn_tflops=4.0 * geo.total * geo.total * HEADS * DIM / (ms * 1e-3) / 1e12,
+                what="wan.self_attention_forward (the hook worker.install_network installs), bf16 Linear layers, "
+                     "pinned-host x in and layer output out each step, serial on one stream")
 
 
 def workload_config(world, total=TOTAL):
