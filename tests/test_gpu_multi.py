@@ -188,3 +188,67 @@ def test_cfg_batch_over_nccl(world, total, heads, exchange, tmp_path, cuda_lib):
     for rank in range(world):
         data = json.loads(Path(f"{report}.{rank}").read_text())
         assert data["ok"], data
+
+
+def layer_worker(rank, world, port, report, total, heads, fin, exchange):
+    """The whole layer (UlyssesAttention.forward_layer: q/k/v GEMM with the
+    RMSNorm/RoPE/pack epilogue storing into the exchange, attention, output
+    GEMM from the exchange buffer) over a real process group, batch of 2,
+    biases on every Linear, against the fp32 layer on this rank's rows."""
+    import sys
+    for p in (str(ROOT), str(ROOT / "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import __graft_entry__
+    __graft_entry__.load_package()
+    from oracle import ulysses_oracle as oracle
+    from powershard_b200.ulysses import UlyssesAttention
+    from test_gpu_layer import assert_layer_close, layer_reference
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        g = torch.Generator().manual_seed(21)
+        hid = heads * 128
+        x = torch.randn(2, total, fin, generator=g).to(torch.bfloat16).to(dev)
+        ws = [(torch.randn(hid, fin, generator=g) * 0.02).to(torch.bfloat16).to(dev) for _ in range(3)]
+        ws.append((torch.randn(fin, hid, generator=g) * 0.02).to(torch.bfloat16).to(dev))
+        bs = [(torch.randn(n, generator=g) * 0.02).to(dev) for n in (hid, hid, hid, fin)]
+        nq = (torch.rand(hid, generator=g) + 0.5).to(dev)
+        nk = (torch.rand(hid, generator=g) + 0.5).to(dev)
+        table = oracle.rope_table_3d((total // 100 + 1, 10, 10), 128)[0, :total, 0].contiguous().to(dev)
+        a, b = oracle.shard_bounds(total, rank, world)
+        engine = UlyssesAttention(exchange=exchange)
+        state = {}
+        out = engine.forward_layer(x[:, a:b].contiguous(), *ws, nq, nk, table[a:b], *bs, total=total, heads=heads,
+                                   out_dtype=torch.float32, state=state)
+        engine.check()
+        ok, msg = True, ""
+        if b > a:
+            for row in range(2):
+                ref = layer_reference(x[row], ws, bs, nq, nk, table, heads)[a:b]
+                try:
+                    assert_layer_close(out[row], ref, ws[3])
+                except AssertionError as exc:
+                    ok, msg = False, str(exc)
+        ok = ok and state["kv_collectives"] == 1 and state["exchange"] == exchange
+        engine.close()
+        Path(f"{report}.{rank}").write_text(json.dumps(dict(ok=ok, msg=msg, rank=rank)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total,heads,fin,exchange", [(2, 1000, 6, 768, "nccl"), (2, 1000, 6, 768, "peer"),
+                                                            (4, 1023, 8, 1024, "peer"), (8, 1500, 40, 512, "peer")])
+def test_layer_over_nccl(world, total, heads, fin, exchange, tmp_path, cuda_lib):
+    """forward_layer with both exchanges on real ranks (the Wan hook's fused
+    path, powershard/wan_model.py:421-438 + 441-502)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"NOT_RUN: needs {world} GPUs, box has {torch.cuda.device_count()}")
+    report = tmp_path / "r"
+    mp.spawn(layer_worker, args=(world, _free_port(), str(report), total, heads, fin, exchange), nprocs=world,
+             join=True)
+    for rank in range(world):
+        data = json.loads(Path(f"{report}.{rank}").read_text())
+        assert data["ok"], data
