@@ -90,8 +90,11 @@ __device__ __forceinline__ float2 block_sum2(float a, float b, float2* red) {
 // vectors per thread each) is issued before any arithmetic, so the row's
 // reads are in flight together; v is stored as soon as it arrives, q and k
 // share one block reduction (full-width norm) and one read of the RoPE table.
+// At most 64 registers for rows of <= 3 vectors per thread: four CTAs per SM
+// keep more rows' loads in flight (9 % faster at configs[1] than three CTAs
+// at 80 registers; at 48 registers the spills cost more than the occupancy).
 template <bool kFp16, int kVec, bool kSplit>
-__global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 3) prepass_kernel(const PrepassArgs a) {
+__global__ void __launch_bounds__(kThreads, kVec >= 4 ? 2 : 4) prepass_kernel(const PrepassArgs a) {
   __shared__ float2 red[kThreads / 32];
   __shared__ uint16_t* sdst[kMaxSegs];
   const int i = blockIdx.x;
