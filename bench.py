@@ -748,7 +748,7 @@ def main():
         # reported in the line instead of ending the run.
         try:
             layer = measure_layer(engine, geo, freqs, dev, world)
-        except (RuntimeError, ValueError) as exc:
+        except Exception as exc:  # noqa: BLE001 - reported in the line, never fatal to the metric
             layer = dict(error=f"{type(exc).__name__}: {str(exc)[:300]}")
 
     cpu = None
