@@ -153,3 +153,40 @@ def test_static_block_rejects_head_dim_before_any_work(lib):
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"head_dim 128" in lib.ps_b200_last_error()
     assert lib.ps_b200_kernel_launches() == 0
+
+
+def test_projection_entries_validate_on_the_host(lib):
+    """The projection GEMM entries (powershard/wan_model.py:425-438 fused with
+    the pre-pass and the unpack) refuse unsupported shapes and bad tables with
+    the documented codes before any device work."""
+    from powershard_b200 import _lib
+
+    def qkv(dtype=_lib.BF16, batch=1, world=2, n_local=100, seg_rows=100, heads=4, hpr=2, head_dim=128, fin=256,
+            eps=1e-6, dst=(16, 16)):
+        table = _lib.ptrs(list(dst)) if dst is not None else None
+        return lib.ps_b200_qkv_proj_batch(16, fin, 16, 16, 16, None, None, None, _lib.FP32, 16, 16, _lib.FP32, 16,
+                                          0, 256, table, dtype, batch, world, n_local, seg_rows, heads, hpr,
+                                          head_dim, fin, eps, None, 0, None, None)
+
+    assert qkv(dtype=_lib.FP32) == _lib.ERR_UNSUPPORTED and b"bf16" in lib.ps_b200_last_error()
+    assert qkv(head_dim=64) == _lib.ERR_UNSUPPORTED and b"head_dim 128" in lib.ps_b200_last_error()
+    assert qkv(heads=3, hpr=2) == _lib.ERR_UNSUPPORTED and b"even head count" in lib.ps_b200_last_error()
+    assert qkv(fin=100) == _lib.ERR_UNSUPPORTED and b"multiple of 64" in lib.ps_b200_last_error()
+    assert qkv(heads=6, hpr=2) == _lib.ERR_INVALID  # 2 ranks x 2 heads cannot hold 6 heads
+    assert qkv(seg_rows=50) == _lib.ERR_INVALID  # a segment shorter than the local rows
+    assert qkv(eps=-1.0) == _lib.ERR_INVALID
+    assert qkv(dst=None) == _lib.ERR_INVALID and b"destination table" in lib.ps_b200_last_error()
+    assert qkv(dst=(16, 24)) == _lib.ERR_INVALID and b"destination block 1" in lib.ps_b200_last_error()
+    assert qkv(batch=0) == _lib.OK  # nothing to do
+    assert lib.ps_b200_qkv_proj_workspace_bytes(100, 4, 128) > 0
+
+    def out(n_local=100, fin=256, fout=256, out_stride=256, block_cols=0, out_dtype=_lib.BF16):
+        return lib.ps_b200_out_proj(16, fin, 0, block_cols, 16, None, _lib.FP32, 16, out_stride, _lib.BF16,
+                                    out_dtype, n_local, fin, fout, None, None)
+
+    assert out(fout=300) == _lib.ERR_UNSUPPORTED and b"out_features" in lib.ps_b200_last_error()
+    assert out(out_dtype=_lib.FP16) == _lib.ERR_UNSUPPORTED
+    assert out(out_stride=128) == _lib.ERR_INVALID
+    assert out(block_cols=100) == _lib.ERR_UNSUPPORTED and b"multiple of 64" in lib.ps_b200_last_error()
+    assert out(n_local=0) == _lib.OK
+    assert lib.ps_b200_kernel_launches() == 0
